@@ -1,0 +1,143 @@
+// The extern "C" entry points of include/gdr.h: argument checks (bunsen's
+// shape contracts, delta_rule.rs:135-150 and :233, become GDR_ERR_INVALID),
+// then the kernel that serves the call.
+#include <cmath>
+
+#include "gdr_common.cuh"
+
+namespace gdr {
+cudaError_t launch_recurrent(const Problem&, int, const void*, const void*, const void*,
+                             const float*, const float*, const float*, void*, float*,
+                             cudaStream_t);
+cudaError_t launch_chunked_ffma(const Problem&, int, const void*, const void*, const void*,
+                                const float*, const float*, const float*, void*, float*,
+                                cudaStream_t);
+bool chunked_ffma_supports(int dk, int dv, int c);
+bool chunked_tc_supports(const gdr_params& p);
+cudaError_t launch_chunked_tc(const Problem&, const void*, const void*, const void*,
+                              const float*, const float*, const float*, void*, float*,
+                              cudaStream_t);
+cudaError_t take_device_error(int* flag);
+}  // namespace gdr
+
+namespace {
+
+using gdr::Problem;
+
+// Checks what the host can check and fills the kernels' descriptor.
+gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Problem& p) {
+    if (params == nullptr) return GDR_ERR_INVALID;
+    const gdr_params& a = *params;
+    if (a.heads_qk <= 0 || a.heads_v <= 0 || a.heads_v % a.heads_qk != 0) return GDR_ERR_INVALID;
+    if (a.d_k <= 0 || a.d_v <= 0 || a.seq_len < 0) return GDR_ERR_INVALID;
+    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16) return GDR_ERR_INVALID;
+    if (a.use_l2norm && !(a.l2norm_eps >= 0.0)) return GDR_ERR_INVALID;
+    if (cu_seqlens == nullptr && a.batch < 0) return GDR_ERR_INVALID;
+    if (cu_seqlens != nullptr && a.n_seqs < 0) return GDR_ERR_INVALID;
+    p.n_seqs = cu_seqlens ? a.n_seqs : a.batch;
+    p.seq_len = a.seq_len;
+    p.cu_seqlens = cu_seqlens;
+    p.heads_qk = a.heads_qk;
+    p.heads_v = a.heads_v;
+    p.group = a.heads_v / a.heads_qk;
+    p.d_k = a.d_k;
+    p.d_v = a.d_v;
+    p.chunk = a.chunk_size;
+    p.use_l2norm = a.use_l2norm != 0;
+    p.l2norm_eps = static_cast<float>(a.l2norm_eps);
+    p.q_scale = 1.0f / std::sqrt(static_cast<float>(a.d_k));
+    if (p.n_seqs > 65535 || p.heads_v > 65535) return GDR_ERR_UNSUPPORTED;  // grid limits
+    return GDR_OK;
+}
+
+bool io_ok(const void* q, const void* k, const void* v, const float* g, const float* beta,
+           const void* out, const float* state_out) {
+    return q && k && v && g && beta && out && state_out;
+}
+
+gdr_status from_cuda(cudaError_t e) { return e == cudaSuccess ? GDR_OK : GDR_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+gdr_status gdr_recurrent(const gdr_params* params, const void* q, const void* k, const void* v,
+                         const float* g, const float* beta, const float* state_in, void* out,
+                         float* state_out, const int32_t* cu_seqlens, void* stream) {
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    if (!io_ok(q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
+    if (p.d_k > 256 || p.d_v > 256) return GDR_ERR_UNSUPPORTED;
+    if (p.n_seqs == 0) return GDR_OK;
+    return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out,
+                                           state_out, static_cast<cudaStream_t>(stream)));
+}
+
+gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, const void* v,
+                       const float* g, const float* beta, const float* state_in, void* out,
+                       float* state_out, const int32_t* cu_seqlens, void* stream) {
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    if (params->chunk_size <= 0) return GDR_ERR_INVALID;  // delta_rule.rs:233
+    if (!io_ok(q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
+    const int algo = params->algo;
+    if (algo != GDR_ALGO_AUTO && algo != GDR_ALGO_CUDA_CORE && algo != GDR_ALGO_TENSOR)
+        return GDR_ERR_INVALID;
+    const bool tc_ok = gdr::chunked_tc_supports(*params);
+    const bool ffma_ok = gdr::chunked_ffma_supports(p.d_k, p.d_v, p.chunk);
+    bool use_tc;
+    if (algo == GDR_ALGO_TENSOR) {
+        if (!tc_ok) return GDR_ERR_UNSUPPORTED;
+        use_tc = true;
+    } else if (algo == GDR_ALGO_CUDA_CORE) {
+        if (!ffma_ok) return GDR_ERR_UNSUPPORTED;
+        use_tc = false;
+    } else {
+        if (!tc_ok && !ffma_ok) return GDR_ERR_UNSUPPORTED;
+        use_tc = tc_ok;
+    }
+    if (p.n_seqs == 0) return GDR_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (use_tc)
+        return from_cuda(gdr::launch_chunked_tc(p, q, k, v, g, beta, state_in, out, state_out, s));
+    return from_cuda(gdr::launch_chunked_ffma(p, params->dtype, q, k, v, g, beta, state_in, out,
+                                              state_out, s));
+}
+
+size_t gdr_mixed_workspace_size(const gdr_params* params) {
+    (void)params;
+    return 0;
+}
+
+gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, const void* v,
+                     const float* g, const float* beta, float* state_pool,
+                     const int32_t* state_slots, void* out, const int32_t* cu_seqlens,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    (void)params, (void)q, (void)k, (void)v, (void)g, (void)beta, (void)state_pool;
+    (void)state_slots, (void)out, (void)cu_seqlens, (void)workspace, (void)workspace_bytes;
+    (void)stream;
+    return GDR_ERR_UNSUPPORTED;
+}
+
+gdr_status gdr_device_error(void) {
+    int flag = 0;
+    if (gdr::take_device_error(&flag) != cudaSuccess) return GDR_ERR_CUDA;
+    return flag ? GDR_ERR_TIMEOUT : GDR_OK;
+}
+
+const char* gdr_status_string(gdr_status status) {
+    switch (status) {
+        case GDR_OK: return "ok";
+        case GDR_ERR_INVALID: return "invalid argument (shape, pointer or option)";
+        case GDR_ERR_UNSUPPORTED: return "no kernel for these dimensions or dtypes";
+        case GDR_ERR_CUDA: return "a CUDA call or launch failed";
+        case GDR_ERR_TIMEOUT: return "a bounded device-side wait ran out";
+    }
+    return "unknown status";
+}
+
+int32_t gdr_abi_version(void) { return GDR_ABI_VERSION; }
+
+}  // extern "C"

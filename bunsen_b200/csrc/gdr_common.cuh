@@ -1,0 +1,65 @@
+// Shared device helpers and the launch descriptor every kernel receives.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gdr.h"
+
+namespace gdr {
+
+// What a kernel needs to address one (sequence, head) of a call. Built on
+// the host from gdr_params by the entry points in gdr_api.cu.
+struct Problem {
+    int32_t n_seqs;           // sequences (dense: B)
+    int32_t seq_len;          // dense T (cu_seqlens == nullptr), else T_total
+    const int32_t* cu_seqlens;  // nullptr: dense, sequence s = [s*T, (s+1)*T)
+    int32_t heads_qk, heads_v, group;  // group = H_v / H_qk
+    int32_t d_k, d_v, chunk;
+    int32_t use_l2norm;
+    float l2norm_eps;
+    float q_scale;  // 1 / sqrt(d_k)
+};
+
+// [start, end) of sequence s in the packed token axis. Offsets are clamped
+// to [0, T_total] so a malformed cu_seqlens can never address outside the
+// caller's buffers.
+__device__ __forceinline__ void seq_span(const Problem& p, int s, int64_t& start, int64_t& end) {
+    if (p.cu_seqlens == nullptr) {
+        start = static_cast<int64_t>(s) * p.seq_len;
+        end = start + p.seq_len;
+        return;
+    }
+    int64_t a = p.cu_seqlens[s], b = p.cu_seqlens[s + 1];
+    a = a < 0 ? 0 : (a > p.seq_len ? p.seq_len : a);
+    b = b < a ? a : (b > p.seq_len ? p.seq_len : b);
+    start = a;
+    end = b;
+}
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+    return __float2bfloat16_rn(x);
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// 1 / (sqrt(sum x^2 + eps)), or 1 without the norm: bunsen's l2norm factor
+// (delta_rule.rs:112-123), applied as a multiplication.
+__device__ __forceinline__ float l2_factor(const Problem& p, float sumsq) {
+    return p.use_l2norm ? 1.0f / sqrtf(sumsq + p.l2norm_eps) : 1.0f;
+}
+
+}  // namespace gdr

@@ -1,0 +1,230 @@
+// GatedDeltaRule::recurrent (delta_rule.rs:182-209) on CUDA cores.
+//
+// Per (sequence, value head) and position t, with S the [d_k, d_v] f32 state:
+//   S <- exp(g_t) S;  read = k_t^T S;  delta = (v_t - read) beta_t;
+//   S <- S + k_t delta^T;  o_t = q_t^T S
+// q_t, k_t L2-normalised (when asked) and q_t scaled by 1/sqrt(d_k).
+//
+// Two kernels:
+//  * recurrent_d128 -- d_k = d_v = 128, the decode hot path. Bandwidth bound:
+//    each state is read from HBM once and written once (64 KiB each way per
+//    head). One CTA of 256 threads per (sequence, head): warp w holds state
+//    rows w, w+8, ..., w+120 and lane l columns 4l..4l+3, in registers, so
+//    every state access is a 128-bit load/store and a warp touches one whole
+//    512-byte row per instruction. The two reductions over d_k (k^T S and
+//    q^T S) run in one pass: o = q^T S_decayed + delta (q . k), which is
+//    q^T S after the rank-one update. One smem exchange per position.
+//  * recurrent_generic -- any d_k, d_v <= 256: the state in shared memory,
+//    one thread per column. For small or unusual head sizes (bunsen's unit
+//    test shapes); not a performance path.
+#include "gdr_common.cuh"
+
+namespace gdr {
+
+namespace {
+
+constexpr int kD = 128;         // d_k = d_v of the fast path
+constexpr int kWarps = 8;       // warps per CTA
+constexpr int kRowsPerWarp = kD / kWarps;  // 16 state rows per thread
+
+template <typename T>
+__global__ void __launch_bounds__(256, 2)
+recurrent_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
+               const T* __restrict__ v, const float* __restrict__ g,
+               const float* __restrict__ beta, const float* state_in, T* __restrict__ out,
+               float* state_out) {
+    const int h = blockIdx.x, s = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int64_t t0, t1;
+    seq_span(p, s, t0, t1);
+
+    __shared__ float qk_raw[2][kD];          // this position's q and k
+    __shared__ float red[2][kWarps][kD];     // per-warp partial k^T S, q^T S
+    __shared__ float delta_s[kD];
+    __shared__ float scal[4];                // q factor, k factor, q.k
+
+    const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
+    const int col = 4 * lane;
+    float st[kRowsPerWarp][4];
+    if (state_in != nullptr) {
+        const float* src = state_in + head_state;
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const float4 x =
+                *reinterpret_cast<const float4*>(src + (warp + kWarps * r) * kD + col);
+            st[r][0] = x.x; st[r][1] = x.y; st[r][2] = x.z; st[r][3] = x.w;
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) st[r][0] = st[r][1] = st[r][2] = st[r][3] = 0.f;
+    }
+
+    const int hq = h / p.group;
+    for (int64_t t = t0; t < t1; ++t) {
+        // q and k of this position, raw, into shared memory.
+        const int64_t qk_off = (t * p.heads_qk + hq) * kD;
+        qk_raw[tid >> 7][tid & 127] = to_f32(((tid < 128) ? q : k)[qk_off + (tid & 127)]);
+        const int64_t gate = t * p.heads_v + h;
+        const float decay = __expf(g[gate]);
+        const float bt = beta[gate];
+        __syncthreads();
+        if (warp < 3) {  // |q|^2, |k|^2, q.k
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a[i] = qk_raw[warp == 1 ? 1 : 0][col + i];
+                b[i] = qk_raw[warp == 0 ? 0 : 1][col + i];
+            }
+            float acc = a[0] * b[0] + a[1] * b[1] + a[2] * b[2] + a[3] * b[3];
+            acc = warp_sum(acc);
+            if (lane == 0) scal[warp == 2 ? 3 : warp] = acc;  // 0: |q|^2 1: |k|^2 3: q.k
+        }
+        __syncthreads();
+        const float fq = l2_factor(p, scal[0]) * p.q_scale;
+        const float fk = l2_factor(p, scal[1]);
+        float pk[4] = {0.f, 0.f, 0.f, 0.f}, pq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const int row = warp + kWarps * r;
+            const float kr = qk_raw[1][row] * fk, qr = qk_raw[0][row] * fq;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                st[r][c] *= decay;
+                pk[c] = fmaf(kr, st[r][c], pk[c]);
+                pq[c] = fmaf(qr, st[r][c], pq[c]);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            red[0][warp][col + c] = pk[c];
+            red[1][warp][col + c] = pq[c];
+        }
+        __syncthreads();
+        if (tid < kD) {
+            float read = 0.f, qs = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                read += red[0][w][tid];
+                qs += red[1][w][tid];
+            }
+            const float vj = to_f32(v[(t * p.heads_v + h) * kD + tid]);
+            const float d = (vj - read) * bt;
+            delta_s[tid] = d;
+            const float qk_dot = scal[3] * fq * fk;
+            out[(t * p.heads_v + h) * kD + tid] = from_f32<T>(fmaf(d, qk_dot, qs));
+        }
+        __syncthreads();
+        float dl[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) dl[c] = delta_s[col + c];
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const float kr = qk_raw[1][warp + kWarps * r] * fk;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) st[r][c] = fmaf(kr, dl[c], st[r][c]);
+        }
+        __syncthreads();  // qk_raw, red and delta_s are rewritten next position
+    }
+
+    float* dst = state_out + head_state;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r)
+        *reinterpret_cast<float4*>(dst + (warp + kWarps * r) * kD + col) =
+            make_float4(st[r][0], st[r][1], st[r][2], st[r][3]);
+}
+
+// Any d_k, d_v <= 256. Shared memory: the state (d_k * d_v f32), q and k.
+template <typename T>
+__global__ void __launch_bounds__(128)
+recurrent_generic(Problem p, const T* __restrict__ q, const T* __restrict__ k,
+                  const T* __restrict__ v, const float* __restrict__ g,
+                  const float* __restrict__ beta, const float* state_in, T* __restrict__ out,
+                  float* state_out) {
+    extern __shared__ float smem[];
+    const int dk = p.d_k, dv = p.d_v;
+    float* S = smem;                 // [dk][dv]
+    float* qv = S + dk * dv;         // [dk]
+    float* kv = qv + dk;             // [dk]
+    __shared__ float norms[2];
+    const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+    int64_t t0, t1;
+    seq_span(p, s, t0, t1);
+    const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * dk * dv;
+    for (int e = tid; e < dk * dv; e += blockDim.x)
+        S[e] = state_in ? state_in[head_state + e] : 0.f;
+    const int hq = h / p.group;
+    for (int64_t t = t0; t < t1; ++t) {
+        const int64_t qk_off = (t * p.heads_qk + hq) * dk;
+        for (int i = tid; i < dk; i += blockDim.x) {
+            qv[i] = to_f32(q[qk_off + i]);
+            kv[i] = to_f32(k[qk_off + i]);
+        }
+        __syncthreads();
+        if (tid < 64) {  // warp 0: |q|^2, warp 1: |k|^2
+            const float* x = tid < 32 ? qv : kv;
+            float acc = 0.f;
+            for (int i = tid & 31; i < dk; i += 32) acc = fmaf(x[i], x[i], acc);
+            acc = warp_sum(acc);
+            if ((tid & 31) == 0) norms[tid >> 5] = acc;
+        }
+        __syncthreads();
+        const float fq = l2_factor(p, norms[0]) * p.q_scale, fk = l2_factor(p, norms[1]);
+        const int64_t gate = t * p.heads_v + h;
+        const float decay = __expf(g[gate]), bt = beta[gate];
+        for (int j = tid; j < dv; j += blockDim.x) {
+            float read = 0.f;
+            for (int i = 0; i < dk; ++i) {
+                S[i * dv + j] *= decay;
+                read = fmaf(kv[i] * fk, S[i * dv + j], read);
+            }
+            const float d = (to_f32(v[(t * p.heads_v + h) * dv + j]) - read) * bt;
+            float o = 0.f;
+            for (int i = 0; i < dk; ++i) {
+                S[i * dv + j] = fmaf(kv[i] * fk, d, S[i * dv + j]);
+                o = fmaf(qv[i] * fq, S[i * dv + j], o);
+            }
+            out[(t * p.heads_v + h) * dv + j] = from_f32<T>(o);
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < dk * dv; e += blockDim.x) state_out[head_state + e] = S[e];
+}
+
+}  // namespace
+
+template <typename T>
+static cudaError_t launch_recurrent_t(const Problem& p, const void* q, const void* k,
+                                      const void* v, const float* g, const float* beta,
+                                      const float* state_in, void* out, float* state_out,
+                                      cudaStream_t stream) {
+    const dim3 grid(p.heads_v, p.n_seqs);
+    if (p.d_k == kD && p.d_v == kD) {
+        recurrent_d128<T><<<grid, 256, 0, stream>>>(
+            p, static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
+            beta, state_in, static_cast<T*>(out), state_out);
+    } else {
+        const size_t smem = sizeof(float) * (p.d_k * p.d_v + 2 * p.d_k);
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(recurrent_generic<T>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+        }
+        recurrent_generic<T><<<grid, 128, smem, stream>>>(
+            p, static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
+            beta, state_in, static_cast<T*>(out), state_out);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_recurrent(const Problem& p, int dtype, const void* q, const void* k,
+                             const void* v, const float* g, const float* beta,
+                             const float* state_in, void* out, float* state_out,
+                             cudaStream_t stream) {
+    if (dtype == GDR_DTYPE_BF16)
+        return launch_recurrent_t<__nv_bfloat16>(p, q, k, v, g, beta, state_in, out, state_out,
+                                                 stream);
+    return launch_recurrent_t<float>(p, q, k, v, g, beta, state_in, out, state_out, stream);
+}
+
+}  // namespace gdr

@@ -1,0 +1,139 @@
+"""``GatedDeltaRule`` over libgdr: the host-side mirror of bunsen's Rust
+operator (``crates/public/bunsen/src/ops/transformers/linear_attention/
+delta_rule.rs:51-310``), on CUDA tensors.
+
+Same options (``qk_l2norm_eps``, ``chunk_size``), same argument order and
+meaning (``q, k, v, g, beta, state``), same returns (the output in ``q``'s
+dtype and the f32 state after the last position), and the same failures: a
+shape that breaks bunsen's contracts (``delta_rule.rs:135-150``) or a zero
+chunk (``:233``) raises before anything launches. Two extensions, both
+opt-in: ``q`` and ``k`` may carry fewer heads than ``v`` (value head ``h``
+reads key head ``h // (H_v // H_qk)``, the arithmetic of the
+``repeat_interleave`` bunsen's caller applies, ``gated_delta_net.rs:404-419``),
+and a packed ragged batch ``[T_total, H, .]`` with ``cu_seqlens``.
+
+Every call runs a CUDA kernel of ``libgdr.so``; there is no other path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.GDR_DTYPE_F32, torch.bfloat16: _lib.GDR_DTYPE_BF16}
+_ALGOS = {"auto": _lib.GDR_ALGO_AUTO, "cuda_core": _lib.GDR_ALGO_CUDA_CORE,
+          "tensor": _lib.GDR_ALGO_TENSOR}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@dataclasses.dataclass(frozen=True)
+class GatedDeltaRule:
+    """The rule's options (``delta_rule.rs:52-60``); the default is bunsen's
+    ``Default``: ``qk_l2norm_eps = Some(1e-6)``, ``chunk_size = 64``."""
+
+    qk_l2norm_eps: float | None = 1e-6
+    chunk_size: int = 64
+    algo: str = "auto"  # chunked calls: "auto", "cuda_core" or "tensor"
+
+    def with_qk_l2norm_eps(self, eps: float | None) -> "GatedDeltaRule":
+        return dataclasses.replace(self, qk_l2norm_eps=eps)
+
+    def with_chunk_size(self, chunk_size: int) -> "GatedDeltaRule":
+        return dataclasses.replace(self, chunk_size=chunk_size)
+
+    # -- the two forms -------------------------------------------------------
+    def recurrent(self, q, k, v, g, beta, state=None, *, cu_seqlens=None, out=None,
+                  state_out=None):
+        """One position at a time (``delta_rule.rs:182-209``)."""
+        return self._run("gdr_recurrent", q, k, v, g, beta, state, cu_seqlens, out, state_out)
+
+    def chunked(self, q, k, v, g, beta, state=None, *, cu_seqlens=None, out=None,
+                state_out=None):
+        """``chunk_size`` positions at a time (``delta_rule.rs:223-310``)."""
+        assert self.chunk_size > 0, "a chunk of at least one position"
+        return self._run("gdr_chunked", q, k, v, g, beta, state, cu_seqlens, out, state_out)
+
+    # -- plumbing ------------------------------------------------------------
+    def params(self, q, v, cu_seqlens) -> _lib.GdrParams:
+        if cu_seqlens is None:
+            b, t, h_qk, d_k = q.shape
+            n = b
+        else:
+            t, h_qk, d_k = q.shape
+            b, n = 0, cu_seqlens.numel() - 1
+        return _lib.GdrParams(
+            batch=b, seq_len=t, n_seqs=n, heads_qk=h_qk, heads_v=v.shape[-2], d_k=d_k,
+            d_v=v.shape[-1], chunk_size=self.chunk_size,
+            use_l2norm=int(self.qk_l2norm_eps is not None),
+            l2norm_eps=float(self.qk_l2norm_eps or 0.0), dtype=_DTYPES[q.dtype],
+            algo=_ALGOS[self.algo])
+
+    def _run(self, fn, q, k, v, g, beta, state, cu_seqlens, out, state_out):
+        packed = cu_seqlens is not None
+        lead = 1 if packed else 2
+        check_shapes(q, k, v, g, beta, state, cu_seqlens)
+        if q.dtype not in _DTYPES:
+            raise TypeError(f"q, k, v in f32 or bf16, not {q.dtype}")
+        dev = q.device
+        if dev.type != "cuda":
+            raise RuntimeError("libgdr runs on CUDA tensors only")
+        g = g.to(torch.float32).contiguous()
+        beta = beta.to(torch.float32).contiguous()
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        n = (cu_seqlens.numel() - 1) if packed else q.shape[0]
+        h_v, d_k, d_v = v.shape[-2], q.shape[-1], v.shape[-1]
+        if out is None:
+            out = torch.empty(v.shape[:lead] + (h_v, d_v), dtype=q.dtype, device=dev)
+        if state_out is None:
+            state_out = torch.empty((n, h_v, d_k, d_v), dtype=torch.float32, device=dev)
+        if state is not None:
+            state = state.to(torch.float32).contiguous()
+        if packed:
+            cu_seqlens = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+        p = self.params(q, v, cu_seqlens)
+        status = getattr(_lib.load(), fn)(
+            ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
+            beta.data_ptr(), _ptr(state), out.data_ptr(), state_out.data_ptr(),
+            _ptr(cu_seqlens), _stream(dev))
+        _lib.check(fn, status)
+        return out, state_out
+
+
+def check_shapes(q, k, v, g, beta, state, cu_seqlens) -> None:
+    """bunsen's shape contracts (``delta_rule.rs:135-150``, ``:323-327``),
+    dense ``[B, T, H, .]`` or packed ``[T_total, H, .]``."""
+    packed = cu_seqlens is not None
+    rank = 3 if packed else 4
+    if q.dim() != rank:
+        raise ValueError(f"q is {'[T, H, Dk]' if packed else '[B, T, H, Dk]'}; got {tuple(q.shape)}")
+    if tuple(k.shape) != tuple(q.shape):
+        raise ValueError(f"k {tuple(k.shape)} must match q {tuple(q.shape)}")
+    lead = tuple(q.shape[: rank - 2])
+    if v.dim() != rank or tuple(v.shape[: rank - 2]) != lead:
+        raise ValueError(f"v {tuple(v.shape)} must share q's leading dims {lead}")
+    h_qk, h_v = q.shape[-2], v.shape[-2]
+    if h_v % h_qk != 0:
+        raise ValueError(f"{h_qk} key heads must divide {h_v} value heads")
+    for name, x in (("g", g), ("beta", beta)):
+        if tuple(x.shape) != lead + (h_v,):
+            raise ValueError(f"the rule's `{name}` is {'[T, H]' if packed else '[B, T, H]'}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("q, k and v share one dtype")
+    if state is not None:
+        n = (cu_seqlens.numel() - 1) if packed else q.shape[0]
+        want = (n, h_v, q.shape[-1], v.shape[-1])
+        if tuple(state.shape) != want:
+            raise ValueError(f"the state is [B, H, Dk, Dv] = {want}; got {tuple(state.shape)}")
+    if packed and (cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1):
+        raise ValueError("cu_seqlens holds n_seqs + 1 offsets")

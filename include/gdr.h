@@ -1,0 +1,147 @@
+/*
+ * gdr.h -- the C ABI of libgdr, a B200 (sm_100a) implementation of bunsen's
+ * gated delta rule.
+ *
+ * Each entry point replaces one method of bunsen's Rust operator
+ * `GatedDeltaRule` (crates/public/bunsen/src/ops/transformers/
+ * linear_attention/delta_rule.rs):
+ *
+ *   gdr_recurrent  <- GatedDeltaRule::recurrent   (delta_rule.rs:182-209)
+ *   gdr_chunked    <- GatedDeltaRule::chunked     (delta_rule.rs:223-310)
+ *   gdr_mixed      <- no single counterpart: one launch that runs what
+ *                     GatedDeltaNet::forward (blocks/transformers/mixers/
+ *                     gated_delta_net.rs:428-433) dispatches per call --
+ *                     `chunked` for prefill segments and `recurrent` for
+ *                     single-token decode rows -- for many sequences at once.
+ *
+ * The argument order is the Rust operator's: q, k, v, g, beta, state; the
+ * rule's options (`qk_l2norm_eps`, `chunk_size`, delta_rule.rs:52-60) travel
+ * in `gdr_params`, as `&self` does in Rust. Results: the output and the state
+ * after the last position.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer (CUDA global memory), except `params`
+ *    and the `gdr_mixed_plan` handle, which live on the host. Nothing here
+ *    allocates device memory except where an entry point says so.
+ *  - `stream` is a `cudaStream_t` passed as `void*` (NULL: the legacy default
+ *    stream). Every call is asynchronous on it; a returned GDR_OK means the
+ *    work was enqueued, not that it finished.
+ *  - Layouts are bunsen's logical layouts, row-major and contiguous:
+ *      q, k        [B, T, H_qk, d_k]   (dense)   or [T_total, H_qk, d_k] (packed)
+ *      v, out      [B, T, H_v,  d_v]             or [T_total, H_v,  d_v]
+ *      g, beta     [B, T, H_v]  f32              or [T_total, H_v]
+ *      state_in,
+ *      state_out   [B, H_v, d_k, d_v] f32        or [n_seqs, H_v, d_k, d_v]
+ *    A dense batch has cu_seqlens == NULL; a packed ragged batch passes
+ *    `cu_seqlens` (device int32, n_seqs + 1 non-decreasing offsets from 0 to
+ *    T_total).
+ *  - Heads: bunsen's rule sees q and k already repeated to H_v heads
+ *    (`repeat_interleave`, ops/repeat.rs:51-66, applied at
+ *    gated_delta_net.rs:404-419). Here q and k keep their H_qk heads and value
+ *    head h reads key head h / (H_v / H_qk), which is the same arithmetic
+ *    without the copy; H_qk == H_v is bunsen's signature exactly.
+ *  - dtypes: q, k, v share `params->dtype`; `out` is written in that dtype
+ *    (bunsen narrows the output to q's dtype, delta_rule.rs:207, 304). g,
+ *    beta and the states are f32, the dtype the rule runs in
+ *    (burner/tensor/widening.rs:60).
+ *  - `state_in` may be NULL (zeros, delta_rule.rs:330). `state_out` may equal
+ *    `state_in` (an in-place update); bunsen itself never writes into a state
+ *    (linear_attention/state.rs:201-204), so a caller that shares states must
+ *    pass a fresh `state_out`.
+ *  - Errors never cross the ABI as exceptions. Bunsen panics on a shape
+ *    mismatch (delta_rule.rs:135-150) or a zero chunk size (:233); here those
+ *    return GDR_ERR_INVALID and launch nothing.
+ */
+#ifndef GDR_H
+#define GDR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDR_ABI_VERSION 1
+
+typedef enum gdr_status {
+    GDR_OK = 0,
+    GDR_ERR_INVALID = 1,     /* bad shape, pointer or option (bunsen: panic) */
+    GDR_ERR_UNSUPPORTED = 2, /* valid, but no kernel for these dims/dtypes   */
+    GDR_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed         */
+    GDR_ERR_TIMEOUT = 4      /* a bounded device-side wait ran out           */
+} gdr_status;
+
+typedef enum gdr_dtype {
+    GDR_DTYPE_F32 = 0,
+    GDR_DTYPE_BF16 = 1
+} gdr_dtype;
+
+/* Which kernel family runs a chunked call. AUTO picks the tensor-core kernel
+ * for bf16, d_k = d_v = 128, chunk 64, and the CUDA-core f32 kernel
+ * otherwise. */
+typedef enum gdr_algo {
+    GDR_ALGO_AUTO = 0,
+    GDR_ALGO_CUDA_CORE = 1, /* f32 FFMA throughout: f32 runs, any small dims */
+    GDR_ALGO_TENSOR = 2     /* tcgen05/TMEM, bf16 operands, f32 accumulate   */
+} gdr_algo;
+
+typedef struct gdr_params {
+    int32_t batch;      /* B of a dense batch; ignored when cu_seqlens != NULL */
+    int32_t seq_len;    /* T of a dense batch, or T_total of a packed one      */
+    int32_t n_seqs;     /* sequences of a packed batch (cu_seqlens has +1)     */
+    int32_t heads_qk;   /* H_qk: key/query heads                               */
+    int32_t heads_v;    /* H_v: value heads, the rule's H; H_qk divides it     */
+    int32_t d_k;        /* key width per head                                  */
+    int32_t d_v;        /* value width per head                                */
+    int32_t chunk_size; /* GatedDeltaRule::chunk_size (bunsen default 64)      */
+    int32_t use_l2norm; /* qk_l2norm_eps is Some(l2norm_eps)                   */
+    double l2norm_eps;  /* bunsen default 1e-6                                 */
+    int32_t dtype;      /* gdr_dtype of q, k, v and out                        */
+    int32_t algo;       /* gdr_algo, chunked calls only                        */
+} gdr_params;
+
+/* The rule one position at a time (GatedDeltaRule::recurrent,
+ * delta_rule.rs:182-209). A decode step is a call with T = 1 (dense) or with
+ * every sequence of length 1 (packed). */
+gdr_status gdr_recurrent(const gdr_params* params, const void* q, const void* k, const void* v,
+                         const float* g, const float* beta, const float* state_in, void* out,
+                         float* state_out, const int32_t* cu_seqlens, void* stream);
+
+/* The rule a chunk at a time (GatedDeltaRule::chunked, delta_rule.rs:223-310).
+ * A sequence's last chunk may be short. Agrees with gdr_recurrent. */
+gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, const void* v,
+                       const float* g, const float* beta, const float* state_in, void* out,
+                       float* state_out, const int32_t* cu_seqlens, void* stream);
+
+/* A continuous batch in one launch: the packed batch of `cu_seqlens`, whose
+ * sequences of length 1 are decode rows (run as gdr_recurrent would) and whose
+ * longer sequences are prefill segments (run as gdr_chunked would). Sequence s
+ * reads and writes its state in place at `state_pool[state_slots[s]]`
+ * ([n_slots, H_v, d_k, d_v] f32); `state_slots` NULL means slot s. A slot
+ * holds its sequence's state on entry (a fresh sequence's slot holds zeros).
+ * Work is scheduled longest-first from a device-side work list that the call
+ * builds in `workspace` (device memory of at least
+ * gdr_mixed_workspace_size(params) bytes, owned by the caller). */
+size_t gdr_mixed_workspace_size(const gdr_params* params);
+gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, const void* v,
+                     const float* g, const float* beta, float* state_pool,
+                     const int32_t* state_slots, void* out, const int32_t* cu_seqlens,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* GDR_ERR_TIMEOUT if a kernel of this library gave up a bounded device-side
+ * wait since the last call (and clears the record), else GDR_OK.
+ * Synchronous: waits for the device's outstanding work. */
+gdr_status gdr_device_error(void);
+
+/* A short English description of a status. */
+const char* gdr_status_string(gdr_status status);
+
+/* GDR_ABI_VERSION of the loaded library. */
+int32_t gdr_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDR_H */

@@ -1,0 +1,100 @@
+"""The C ABI without a GPU: the library loads, exports every function
+include/gdr.h declares, lays out gdr_params as the header does, and rejects
+bad arguments (bunsen's panics, delta_rule.rs:135-150, :233) before touching
+the device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+
+from bunsen_b200 import _lib
+from tests.conftest import ROOT
+
+HEADER = ROOT / "include" / "gdr.h"
+
+
+def declared() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(gdr_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function():
+    lib = _lib.load()
+    names = declared()
+    assert {"gdr_recurrent", "gdr_chunked", "gdr_mixed"} <= set(names)
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (gdr_\w+)", out))
+    assert set(names) <= exported
+
+
+def test_params_layout_matches_header(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "gdr.h"\n'
+        "int main(void) { printf(\"%zu" + " %zu" * 12 + "\\n\", sizeof(gdr_params)"
+        + "".join(f", offsetof(gdr_params, {f})" for f, _ in _lib.GdrParams._fields_)
+        + "); return 0; }\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), "-o", str(exe), str(src)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    want = [ctypes.sizeof(_lib.GdrParams)] + [getattr(_lib.GdrParams, f).offset
+                                              for f, _ in _lib.GdrParams._fields_]
+    assert got == want
+
+
+def test_abi_version_and_status_strings():
+    lib = _lib.load()
+    assert lib.gdr_abi_version() == 1
+    for s in range(5):
+        assert lib.gdr_status_string(s)
+    assert lib.gdr_status_string(99) == b"unknown status"
+
+
+def _params(**kw):
+    base = dict(batch=1, seq_len=4, n_seqs=0, heads_qk=2, heads_v=4, d_k=8, d_v=8, chunk_size=4,
+                use_l2norm=1, l2norm_eps=1e-6, dtype=_lib.GDR_DTYPE_F32, algo=0)
+    base.update(kw)
+    return _lib.GdrParams(**base)
+
+
+@pytest.mark.parametrize("fn", ["gdr_recurrent", "gdr_chunked"])
+@pytest.mark.parametrize("bad", [dict(heads_v=3), dict(heads_qk=0), dict(d_k=0), dict(dtype=7),
+                                 dict(batch=-1), dict(use_l2norm=1, l2norm_eps=-1.0)])
+def test_invalid_arguments_are_rejected_before_launch(fn, bad):
+    lib = _lib.load()
+    p = _params(**bad)
+    dummy = ctypes.c_void_p(16)  # never dereferenced: the checks come first
+    st = getattr(lib, fn)(ctypes.byref(p), dummy, dummy, dummy, dummy, dummy, None, dummy, dummy,
+                          None, None)
+    assert st == _lib.GDR_ERR_INVALID
+
+
+def test_null_pointers_and_zero_chunk_are_rejected():
+    lib = _lib.load()
+    d = ctypes.c_void_p(16)
+    assert lib.gdr_chunked(None, d, d, d, d, d, None, d, d, None, None) == _lib.GDR_ERR_INVALID
+    p = _params()
+    assert lib.gdr_chunked(ctypes.byref(p), None, d, d, d, d, None, d, d, None,
+                           None) == _lib.GDR_ERR_INVALID
+    p = _params(chunk_size=0)
+    assert lib.gdr_chunked(ctypes.byref(p), d, d, d, d, d, None, d, d, None,
+                           None) == _lib.GDR_ERR_INVALID
+
+
+def test_tensor_path_needs_its_shapes():
+    """The tensor-core kernel serves bf16, d_k = d_v = 128, chunk 64 only;
+    asking it for anything else is GDR_ERR_UNSUPPORTED, not a fallback."""
+    lib = _lib.load()
+    d = ctypes.c_void_p(16)
+    p = _params(algo=_lib.GDR_ALGO_TENSOR)
+    assert lib.gdr_chunked(ctypes.byref(p), d, d, d, d, d, None, d, d, None,
+                           None) == _lib.GDR_ERR_UNSUPPORTED
