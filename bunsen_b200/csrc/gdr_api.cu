@@ -24,6 +24,10 @@ namespace {
 
 using gdr::Problem;
 
+int64_t total_tokens(const Problem& p) {
+    return p.cu_seqlens ? p.seq_len : static_cast<int64_t>(p.n_seqs) * p.seq_len;
+}
+
 // Checks what the host can check and fills the kernels' descriptor.
 gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Problem& p) {
     if (params == nullptr) return GDR_ERR_INVALID;
@@ -50,9 +54,12 @@ gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Pro
     return GDR_OK;
 }
 
-bool io_ok(const void* q, const void* k, const void* v, const float* g, const float* beta,
-           const void* out, const float* state_out) {
-    return q && k && v && g && beta && out && state_out;
+// Token buffers may be NULL only when there are no tokens (an empty tensor
+// has no storage); the state is written whenever there are sequences.
+bool io_ok(const Problem& p, const void* q, const void* k, const void* v, const float* g,
+           const float* beta, const void* out, const float* state_out) {
+    const bool tokens = total_tokens(p) > 0;
+    return (!tokens || (q && k && v && g && beta && out)) && (p.n_seqs == 0 || state_out);
 }
 
 gdr_status from_cuda(cudaError_t e) { return e == cudaSuccess ? GDR_OK : GDR_ERR_CUDA; }
@@ -67,7 +74,7 @@ gdr_status gdr_recurrent(const gdr_params* params, const void* q, const void* k,
     Problem p;
     gdr_status st = make_problem(params, cu_seqlens, p);
     if (st != GDR_OK) return st;
-    if (!io_ok(q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
+    if (!io_ok(p, q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
     if (p.d_k > 256 || p.d_v > 256) return GDR_ERR_UNSUPPORTED;
     if (p.n_seqs == 0) return GDR_OK;
     return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out,
@@ -81,7 +88,7 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
     gdr_status st = make_problem(params, cu_seqlens, p);
     if (st != GDR_OK) return st;
     if (params->chunk_size <= 0) return GDR_ERR_INVALID;  // delta_rule.rs:233
-    if (!io_ok(q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
+    if (!io_ok(p, q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
     const int algo = params->algo;
     if (algo != GDR_ALGO_AUTO && algo != GDR_ALGO_CUDA_CORE && algo != GDR_ALGO_TENSOR)
         return GDR_ERR_INVALID;
@@ -100,6 +107,9 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
     }
     if (p.n_seqs == 0) return GDR_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (total_tokens(p) == 0)  // nothing to run: the state passes through
+        return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out,
+                                               state_out, s));
     if (use_tc)
         return from_cuda(gdr::launch_chunked_tc(p, q, k, v, g, beta, state_in, out, state_out, s));
     return from_cuda(gdr::launch_chunked_ffma(p, params->dtype, q, k, v, g, beta, state_in, out,

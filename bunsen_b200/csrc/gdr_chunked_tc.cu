@@ -1,28 +1,32 @@
 // GatedDeltaRule::chunked (delta_rule.rs:223-310) on the sm_100a tensor cores.
 //
 // bf16 q/k/v, d_k = d_v = 128, chunk C = 64; f32 g, beta, state, f32
-// accumulation everywhere. One CTA (128 threads, one TMEM lane each) per
-// (sequence, value head) walks the sequence's chunks in order; the state
-// lives in TMEM for the whole sequence and touches HBM once on each end.
+// accumulation everywhere. One CTA (256 threads) per (sequence, value head)
+// walks the sequence's chunks in order; the state lives in TMEM for the whole
+// sequence and touches HBM once on each end. Two CTAs share an SM.
 //
 // Every contraction of a chunk is one tcgen05.mma group with M = 128 (the
 // feature axis, or the 64 keys stacked on the 64 queries), so the tensor
 // core always runs full-height tiles. The state is kept transposed,
 // S^T [d_v, d_k], so that it is the accumulator of its own update:
 //
-//   G1  [K;Q] K^T            -> TMEM R0 [128 x 64]   Gram of keys / queries
-//        (CUDA cores: norms, decay mask, L = strict_lower(.), intra,
-//         A = (I + L)^-1 by a blocked forward substitution)
+//   G1  [K;Q] [K;Q]^T       -> TMEM G [128 x 128]  Gram of keys and queries
+//        (CUDA cores: norms from its diagonal, decay mask, L =
+//         strict_lower(.), intra; A = (I + L)^-1: exact 16 x 16 diagonal
+//         blocks by forward substitution, off-diagonal blocks by tf32
+//         mma.sync)
 //   G2  V^T (A diag(beta))^T                -> R1  U^T       [d_v x C]
 //       K^T (A diag(beta e^gamma / |k|))^T  -> R0  W^T       [d_k x C]
-//        (CUDA cores: S^T -> bf16 operand, S^T <- e^gamma_C S^T; W^T -> bf16)
+//        (CUDA cores, while G2 runs: S^T -> bf16 operand, S^T <- e^gamma_C
+//         S^T; then W^T -> bf16)
 //   G3  R1 += -(S^T W^T)        V_new^T = U^T - (W S)^T
 //       S^T Q^T                 -> R0  (Q S)^T
 //        (CUDA cores: V_new^T -> bf16, and a copy scaled by e^(gamma_C -
 //         gamma_t) / |k_t| per position)
 //   G4  V_new^T intra^T         -> R1  (intra V_new)^T
 //   G5  S^T += (V_new^T o r) K  the state update
-//        (CUDA cores: O^T = (Q S)^T diag(e^gamma / |q| sqrt(d_k)) + R1)
+//        (CUDA cores, while the next chunk's tiles load:
+//         O^T = (Q S)^T diag(e^gamma / |q| sqrt(d_k)) + R1)
 //
 // q and k enter the tensor core raw; their L2 norms (delta_rule.rs:112-123)
 // and the 1/sqrt(d_k) scale are applied as per-position factors on the
@@ -30,13 +34,17 @@
 // sequence's end take beta = g = 0, which makes them write nothing
 // (delta_rule.rs:241-262), whatever the tile holds there.
 //
+// Threads: warp w serves TMEM lanes 32 (w % 4) .. +31 (one matrix row per
+// thread) and column half w / 4 of every 64-column region.
+//
 // Operand tiles are 128-byte swizzled; TMA writes the input tiles, the
 // CUDA-core stages write the rest with the same swizzle. Shared memory:
 //   KQ  32 KiB  [k-block][K rows 0-63 | Q rows 64-127] x 128 B  (TMA)
-//   VB  16 KiB  V (TMA) -> W^T operand -> output staging
-//   AB  16 KiB  A diag(beta) | A diag(beta e^gamma/|k|) -> intra operand
-//   ST  32 KiB  solve scratch (f32) -> S^T operand -> V_new^T operands
-// ~98 KiB, so two CTAs share an SM (and its 512 TMEM columns).
+//   VB  16 KiB  V (TMA) -> W^T operand
+//   AB  16 KiB  mma.sync scratch -> A diag(beta) | A diag(beta e^gamma/|k|)
+//   IN   8 KiB  intra operand
+//   ST  36 KiB  L and A in f32 -> S^T operand -> V_new^T operands -> output
+//               staging
 #include <cudaTypedefs.h>
 
 #include "gdr_common.cuh"
@@ -50,26 +58,30 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kC = 64;       // chunk
-constexpr int kD = 128;      // d_k = d_v
-constexpr int kThreads = 128;
+constexpr int kC = 64;   // chunk
+constexpr int kD = 128;  // d_k = d_v
+constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0, kColR0 = 128, kColR1 = 192;
+constexpr uint32_t kColS = 0, kColG = 128, kColR0 = 128, kColR1 = 192;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-constexpr uint32_t kOffKQ = 0, kOffVB = 32768, kOffAB = 49152, kOffST = 65536;
-constexpr uint32_t kOffMisc = 98304;
-constexpr uint32_t kTileBytes = 8192;  // one 64 x 64 bf16 TMA box
-constexpr uint32_t kSmemBytes = kOffMisc + 2048 + 1024;  // + alignment slack
+constexpr int kLd = 68;  // f32 row stride of L and A (conflict-free fragments)
+constexpr uint32_t kOffKQ = 0, kOffVB = 32768, kOffAB = 49152, kOffIN = 65536;
+constexpr uint32_t kOffST = 73728, kOffMisc = 110592;
+constexpr uint32_t kOffX = kC * kLd * 4;  // A after L inside ST
+constexpr uint32_t kTileBytes = 8192;     // one 64 x 64 bf16 TMA box
+constexpr uint32_t kSmemBytes = kOffMisc + 3072 + 1024;  // + alignment slack
+constexpr float kLog2e = 1.4426950408889634f;
 
 struct Misc {
-    float gam[kC];   // cumulative log decay within the chunk
-    float bet[kC];   // beta (0 past the end)
-    float fk[kC];    // 1 / |k_t|
-    float fq[kC];    // 1 / (|q_t| sqrt(d_k))
-    float wk[kC];    // beta_t e^gamma_t / |k_t|
-    float rr[kC];    // e^(gamma_C - gamma_t) / |k_t|
-    float cq[kC];    // e^gamma_t / (|q_t| sqrt(d_k))
+    float gam[kC];  // cumulative log decay within the chunk
+    float gl[kC];   // the same in log2 units
+    float bet[kC];  // beta (0 past the end)
+    float fk[kC];   // 1 / |k_t|
+    float fq[kC];   // 1 / (|q_t| sqrt(d_k))
+    float wk[kC];   // beta_t e^gamma_t / |k_t|
+    float rr[kC];   // e^(gamma_C - gamma_t) / |k_t|
+    float cq[kC];   // e^gamma_t / (|q_t| sqrt(d_k))
     uint64_t bar_tma, bar_mma;
     uint32_t tmem_base;
     int failed;
@@ -80,95 +92,127 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&x);
 }
 
-// Writes 64 f32 values as one 128-byte swizzled row (8 chunks of 8 bf16).
-__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const float* x) {
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Writes 32 f32 values as bf16 into 16-byte chunks c0 .. c0+3 of a 128-byte
+// swizzled row.
+__device__ __forceinline__ void store_half_row_sw128(uint8_t* tile, int row, int c0,
+                                                     const float* x) {
     uint8_t* base = tile + row * 128;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
         uint4 v;
         v.x = pack_bf16(x[8 * c + 0], x[8 * c + 1]);
         v.y = pack_bf16(x[8 * c + 2], x[8 * c + 3]);
         v.z = pack_bf16(x[8 * c + 4], x[8 * c + 5]);
         v.w = pack_bf16(x[8 * c + 6], x[8 * c + 7]);
-        *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(base + (((c0 + c) ^ (row & 7)) << 4)) = v;
     }
 }
 
-// Sum of squares of a 128-element bf16 row stored as two 128-B swizzled
-// halves (the swizzle only permutes 16-B chunks within a row).
-__device__ __forceinline__ float row_sumsq(const uint8_t* half0, const uint8_t* half1) {
-    float acc = 0.f;
+__device__ __forceinline__ void load2x32(uint32_t taddr, float (&x)[64]) {
+    float a[32], b[32];
+    tmem_ld32(taddr, a);
+    tmem_ld32(taddr + 32, b);
+    tmem_wait_ld();
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint4* p = reinterpret_cast<const uint4*>(h ? half1 : half0);
+    for (int i = 0; i < 32; ++i) {
+        x[i] = a[i];
+        x[32 + i] = b[i];
+    }
+}
+
+// ---- the unit lower-triangular inverse ---------------------------------------
+__device__ __forceinline__ uint32_t tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+// c[nt] (16 x 8 tiles nt = 0, 1) += A (16 x 16) B (16 x 16), f32 in shared
+// memory with row strides lda, ldb, through tf32 mma.sync.
+__device__ __forceinline__ void mma16_tf32(const float* A, int lda, const float* B, int ldb,
+                                           float (&c)[2][4], int lane) {
+    const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint4 u = p[c];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int ks = 0; ks < 2; ++ks) {
+        const uint32_t a0 = tf32(A[g * lda + 8 * ks + t]);
+        const uint32_t a1 = tf32(A[(g + 8) * lda + 8 * ks + t]);
+        const uint32_t a2 = tf32(A[g * lda + 8 * ks + t + 4]);
+        const uint32_t a3 = tf32(A[(g + 8) * lda + 8 * ks + t + 4]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-                acc = fmaf(f.x, f.x, acc);
-                acc = fmaf(f.y, f.y, acc);
-            }
+        for (int nt = 0; nt < 2; ++nt) {
+            const uint32_t b0 = tf32(B[(8 * ks + t) * ldb + 8 * nt + g]);
+            const uint32_t b1 = tf32(B[(8 * ks + t + 4) * ldb + 8 * nt + g]);
+            asm volatile(
+                "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+                "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+                : "+f"(c[nt][0]), "+f"(c[nt][1]), "+f"(c[nt][2]), "+f"(c[nt][3])
+                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
         }
     }
-    return acc;
 }
 
-// A = (I + L)^-1 for the strictly lower 64 x 64 L in `Lf` (f32, row-major),
-// into `X` (f32, row-major, zero above the diagonal). 16 x 16 diagonal
-// blocks by forward substitution, then the off-diagonal blocks level by
-// level: X_ij = -X_ii sum_{k=j}^{i-1} L_ik X_kj. `Tm` holds 3 16 x 16 f32
-// blocks of scratch.
+__device__ __forceinline__ void store16(float* M, int ld, const float (&c)[2][4], float sign,
+                                        int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+        M[g * ld + 8 * nt + 2 * t] = sign * c[nt][0];
+        M[g * ld + 8 * nt + 2 * t + 1] = sign * c[nt][1];
+        M[(g + 8) * ld + 8 * nt + 2 * t] = sign * c[nt][2];
+        M[(g + 8) * ld + 8 * nt + 2 * t + 1] = sign * c[nt][3];
+    }
+}
+
+// A = (I + L)^-1 for the strictly lower 64 x 64 L in `Lf` into `X` (both f32,
+// row stride kLd; X zero above the diagonal). The 16 x 16 diagonal blocks by
+// exact forward substitution; then the blocks below, one diagonal at a time,
+// X_ij = -X_ii sum_{k=j}^{i-1} L_ik X_kj, with tf32 mma.sync. `Tm` holds 16 x
+// 24 f32 of scratch per warp for 3 warps.
 __device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Tm, int tid) {
+    const int warp = tid >> 5, lane = tid & 31;
     if (tid < 64) {
         const int b = tid >> 4, m = tid & 15;
-        const float* Lb = Lf + (16 * b) * kC + 16 * b;
+        const float* Lb = Lf + (16 * b) * kLd + 16 * b;
         float x[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            float acc = (r == m) ? 1.f : 0.f;
+        for (int r = 0; r < 16; ++r) x[r] = (r == m) ? 1.f : 0.f;
 #pragma unroll
-            for (int j = 0; j < r; ++j) acc = fmaf(-Lb[r * kC + j], x[j], acc);
-            x[r] = acc;
-        }
+        for (int s = 0; s < 15; ++s)
 #pragma unroll
-        for (int r = 0; r < 16; ++r) X[(16 * b + r) * kC + 16 * b + m] = x[r];
+            for (int r = s + 1; r < 16; ++r) x[r] = fmaf(-Lb[r * kLd + s], x[s], x[r]);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) X[(16 * b + r) * kLd + 16 * b + m] = x[r];
     } else {
-        // Zero every block above the block diagonal.
-        for (int e = tid - 64; e < kC * kC; e += 64) {
-            const int i = e / kC, j = e % kC;
-            if ((j >> 4) > (i >> 4)) X[e] = 0.f;
+        // The six blocks above the block diagonal are zero.
+        for (int e = tid - 64; e < 6 * 256; e += kThreads - 64) {
+            const int blk = e >> 8, r = (e >> 4) & 15, c = e & 15;
+            const int ib = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+            const int jb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+            X[(16 * ib + r) * kLd + 16 * jb + c] = 0.f;
         }
     }
     __syncthreads();
-    // Levels 1..3: blocks (j + lvl, j).
 #pragma unroll 1
     for (int lvl = 1; lvl < 4; ++lvl) {
-        const int nblk = 4 - lvl;
-        for (int e = tid; e < nblk * 256; e += kThreads) {
-            const int jb = e >> 8, r = (e >> 4) & 15, c = e & 15;
-            const int ib = jb + lvl;
-            float acc = 0.f;
-            for (int kb = jb; kb < ib; ++kb) {
-                const float* Lrow = Lf + (16 * ib + r) * kC + 16 * kb;
-                const float* Xcol = X + (16 * kb) * kC + 16 * jb + c;
-#pragma unroll
-                for (int k = 0; k < 16; ++k) acc = fmaf(Lrow[k], Xcol[k * kC], acc);
-            }
-            Tm[e] = acc;
-        }
-        __syncthreads();
-        for (int e = tid; e < nblk * 256; e += kThreads) {
-            const int jb = e >> 8, r = (e >> 4) & 15, c = e & 15;
-            const int ib = jb + lvl;
-            const float* Xrow = X + (16 * ib + r) * kC + 16 * ib;
-            const float* T = Tm + (jb << 8) + c;
-            float acc = 0.f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) acc = fmaf(Xrow[k], T[k * 16], acc);
-            X[(16 * ib + r) * kC + 16 * jb + c] = -acc;
+        if (warp < 4 - lvl) {
+            const int jb = warp, ib = jb + lvl;
+            float* T = Tm + warp * 16 * 24;
+            float c[2][4] = {};
+#pragma unroll 1
+            for (int kb = jb; kb < ib; ++kb)
+                mma16_tf32(Lf + (16 * ib) * kLd + 16 * kb, kLd, X + (16 * kb) * kLd + 16 * jb, kLd,
+                           c, lane);
+            store16(T, 24, c, 1.f, lane);
+            __syncwarp();
+            float d[2][4] = {};
+            mma16_tf32(X + (16 * ib) * kLd + 16 * ib, kLd, T, 24, d, lane);
+            store16(X + (16 * ib) * kLd + 16 * jb, kLd, d, -1.f, lane);
         }
         __syncthreads();
     }
@@ -185,10 +229,15 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     uint8_t* KQ = smem + kOffKQ;
     uint8_t* VB = smem + kOffVB;
     uint8_t* AB = smem + kOffAB;
+    uint8_t* IN = smem + kOffIN;
     uint8_t* ST = smem + kOffST;
     Misc& ms = *reinterpret_cast<Misc*>(smem + kOffMisc);
+    float* Lf = reinterpret_cast<float*>(ST);
+    float* X = reinterpret_cast<float*>(ST + kOffX);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int qd = warp & 3, hf = warp >> 2;
+    const int row = 32 * qd + lane;  // this thread's TMEM lane
     const int h = blockIdx.x, s = blockIdx.y;
     const int hq = h / p.group;
     int64_t t0, t1;
@@ -210,20 +259,54 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = ms.tmem_base;
-    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(warp * 32) << 16);
-    const uint32_t tS = lane_addr + kColS, tR0 = lane_addr + kColR0, tR1 = lane_addr + kColR1;
+    const uint32_t lane_addr = tbase + (static_cast<uint32_t>(qd * 32) << 16);
+    const uint32_t sKQ = smem_u32(KQ), sVB = smem_u32(VB), sAB = smem_u32(AB);
+    const uint32_t sIN = smem_u32(IN), sST = smem_u32(ST);
+
+    auto issue_tiles = [&](int ci) {  // thread 0: chunk ci's K, Q, V tiles
+        fence_proxy_async();
+        mbar_expect_tx(&ms.bar_tma, 6 * kTileBytes);
+        const int tok = static_cast<int>(t0 + static_cast<int64_t>(ci) * kC);
+        tma_load_3d(KQ + 0 * kTileBytes, &tm_k, &ms.bar_tma, 0, hq, tok);
+        tma_load_3d(KQ + 1 * kTileBytes, &tm_q, &ms.bar_tma, 0, hq, tok);
+        tma_load_3d(KQ + 2 * kTileBytes, &tm_k, &ms.bar_tma, 64, hq, tok);
+        tma_load_3d(KQ + 3 * kTileBytes, &tm_q, &ms.bar_tma, 64, hq, tok);
+        tma_load_3d(VB + 0 * kTileBytes, &tm_v, &ms.bar_tma, 0, h, tok);
+        tma_load_3d(VB + 1 * kTileBytes, &tm_v, &ms.bar_tma, 64, h, tok);
+        if (ci + 1 < n_chunks) {
+            const int nt = tok + kC;
+            tma_prefetch_3d(&tm_k, 0, hq, nt);
+            tma_prefetch_3d(&tm_k, 64, hq, nt);
+            tma_prefetch_3d(&tm_q, 0, hq, nt);
+            tma_prefetch_3d(&tm_q, 64, hq, nt);
+            tma_prefetch_3d(&tm_v, 0, h, nt);
+            tma_prefetch_3d(&tm_v, 64, h, nt);
+        }
+    };
+    // The gates of chunk ci, zero past the end (tid < 64).
+    auto load_gates = [&](int ci, float& pg, float& pb) {
+        const int64_t pos = static_cast<int64_t>(ci) * kC + tid;
+        const bool in = pos < len;
+        const int64_t gi = (t0 + pos) * p.heads_v + h;
+        pg = in ? g[gi] : 0.f;
+        pb = in ? beta[gi] : 0.f;
+    };
+
+    if (tid == 0 && n_chunks > 0) issue_tiles(0);
+    float pg = 0.f, pb = 0.f;
+    if (tid < kC && n_chunks > 0) load_gates(0, pg, pb);
 
     // The initial state, transposed into TMEM: lane d holds S[:, d].
     const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
     {
-        const int d = tid;
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int cb = 0; cb < 2; ++cb) {
             float x[32];
+            const int c0 = 64 * hf + 32 * cb;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                x[i] = state_in ? state_in[head_state + (cb * 32 + i) * kD + d] : 0.f;
-            tmem_st32(tS + cb * 32, x);
+                x[i] = state_in ? state_in[head_state + (c0 + i) * kD + row] : 0.f;
+            tmem_st32(lane_addr + kColS + c0, x);
         }
         tmem_wait_st();
     }
@@ -232,9 +315,6 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 
     uint32_t ph_tma = 0, ph_mma = 0;
     bool ok = true;
-    const uint32_t sKQ = smem_u32(KQ), sVB = smem_u32(VB), sAB = smem_u32(AB), sST = smem_u32(ST);
-
-    // Waits on an mbarrier phase; on time-out records it and stops the walk.
     auto wait = [&](uint64_t* bar, uint32_t& ph) {
         if (!mbar_wait(bar, ph, kWaitLimitNs)) {
             ms.failed = 1;
@@ -246,36 +326,12 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 #pragma unroll 1
     for (int ci = 0; ci < n_chunks && ok; ++ci) {
         const int64_t tok0 = t0 + static_cast<int64_t>(ci) * kC;
-        const int valid = static_cast<int>(len - static_cast<int64_t>(ci) * kC < kC
-                                               ? len - static_cast<int64_t>(ci) * kC
-                                               : kC);
-        // (1) The chunk's tiles: K and Q stacked per 64-wide k-block, then V.
-        if (tid == 0) {
-            fence_proxy_async();
-            mbar_expect_tx(&ms.bar_tma, 6 * kTileBytes);
-            const int tok = static_cast<int>(tok0);
-            tma_load_3d(KQ + 0 * kTileBytes, &tm_k, &ms.bar_tma, 0, hq, tok);
-            tma_load_3d(KQ + 1 * kTileBytes, &tm_q, &ms.bar_tma, 0, hq, tok);
-            tma_load_3d(KQ + 2 * kTileBytes, &tm_k, &ms.bar_tma, 64, hq, tok);
-            tma_load_3d(KQ + 3 * kTileBytes, &tm_q, &ms.bar_tma, 64, hq, tok);
-            tma_load_3d(VB + 0 * kTileBytes, &tm_v, &ms.bar_tma, 0, h, tok);
-            tma_load_3d(VB + 1 * kTileBytes, &tm_v, &ms.bar_tma, 64, h, tok);
-            if (ci + 1 < n_chunks) {
-                const int nt = tok + kC;
-                tma_prefetch_3d(&tm_k, 0, hq, nt);
-                tma_prefetch_3d(&tm_k, 64, hq, nt);
-                tma_prefetch_3d(&tm_q, 0, hq, nt);
-                tma_prefetch_3d(&tm_q, 64, hq, nt);
-                tma_prefetch_3d(&tm_v, 0, h, nt);
-                tma_prefetch_3d(&tm_v, 64, h, nt);
-            }
-        }
-        // (2) Gates, zero past the end; the cumulative decay by a warp scan.
+        const int64_t left = len - static_cast<int64_t>(ci) * kC;
+        const int valid = static_cast<int>(left < kC ? left : kC);
+        // (a) Gates; the cumulative decay by a warp scan.
         if (tid < kC) {
-            const bool in = tid < valid;
-            const int64_t gi = (tok0 + tid) * p.heads_v + h;
-            ms.gam[tid] = in ? g[gi] : 0.f;
-            ms.bet[tid] = in ? beta[gi] : 0.f;
+            ms.gam[tid] = pg;
+            ms.bet[tid] = pb;
         }
         __syncthreads();
         if (warp == 0) {
@@ -289,153 +345,139 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             const float excl = incl - (a + b);
             ms.gam[2 * lane] = excl + a;
             ms.gam[2 * lane + 1] = excl + a + b;
+            ms.gl[2 * lane] = (excl + a) * kLog2e;
+            ms.gl[2 * lane + 1] = (excl + a + b) * kLog2e;
         }
+        // (b)+(c) The tiles, then G1: [K;Q] [K;Q]^T -> G.
         wait(&ms.bar_tma, ph_tma);
-        // (3) Query norms from the raw Q rows (threads 64..127, row tid-64).
-        if (tid >= kC) {
-            const int i = tid - kC;
-            const float ss = row_sumsq(KQ + 1 * kTileBytes + i * 128, KQ + 3 * kTileBytes + i * 128);
-            ms.fq[i] = l2_factor(p, ss) * p.q_scale;
-        }
-        // (4) G1: [K;Q] K^T -> R0.
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t id = idesc_bf16(128, 64, 0, 0, 0);
+            const uint32_t id = idesc_bf16(128, 128, 0, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColR0, sdesc_sw128(sKQ + off, 16, 1024),
+                umma_bf16(tbase + kColG, sdesc_sw128(sKQ + off, 16, 1024),
                           sdesc_sw128(sKQ + off, 16, 1024), id, ks > 0);
             }
             umma_commit(&ms.bar_mma);
         }
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
-        // (5) Gram rows: lanes 0-63 k_i . k_j, lanes 64-127 q_i . k_j.
-        float row[kC];
-        {
-            float a[32], b[32];
-            tmem_ld32(tR0, a);
-            tmem_ld32(tR0 + 32, b);
+        // (e) This thread's 32 Gram columns, and the norms from the diagonal.
+        float gr[32];
+        tmem_ld32(lane_addr + kColG + 32 * hf, gr);
+        if (qd >= 2 && hf == 0) {
+            float dq[32];
+            tmem_ld32(lane_addr + kColG + 32 * qd, dq);  // q_i . q_i at column 64 + i
             tmem_wait_ld();
+            float d = 0.f;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                row[j] = a[j];
-                row[32 + j] = b[j];
-            }
+            for (int j = 0; j < 32; ++j) d = (j == lane) ? dq[j] : d;
+            ms.fq[row - kC] = l2_factor(p, d) * p.q_scale;
         }
-        if (tid < kC) {
-            float diag = 0.f;
+        tmem_wait_ld();
+        if (qd < 2 && hf == qd) {
+            float d = 0.f;
 #pragma unroll
-            for (int j = 0; j < kC; ++j)
-                if (j == tid) diag = row[j];
-            ms.fk[tid] = l2_factor(p, diag);
+            for (int j = 0; j < 32; ++j) d = (j == lane) ? gr[j] : d;
+            ms.fk[row] = l2_factor(p, d);
         }
+        tc_fence_before();
         __syncthreads();
-        float* Lf = reinterpret_cast<float*>(ST);
-        float* X = reinterpret_cast<float*>(ST + 16384);
-        float* Tm = reinterpret_cast<float*>(AB);
+        // (f) Per-position factors; rows of L (f32) and of intra (bf16 operand).
         if (tid < kC) {
-            const int i = tid;
-            const float gi = ms.gam[i], ci_ = ms.bet[i] * ms.fk[i];
-            float* Lrow = Lf + i * kC;
-#pragma unroll
-            for (int j = 0; j < kC; ++j)
-                Lrow[j] = (j < i) ? ci_ * ms.fk[j] * row[j] * __expf(gi - ms.gam[j]) : 0.f;
-            const float last = ms.gam[kC - 1];
-            ms.wk[i] = ms.bet[i] * __expf(gi) * ms.fk[i];
-            ms.rr[i] = __expf(last - gi) * ms.fk[i];
-        } else {
-            const int i = tid - kC;
-            const float gi = ms.gam[i], fqi = ms.fq[i];
-#pragma unroll
-            for (int j = 0; j < kC; ++j)
-                row[j] = (j <= i) ? fqi * ms.fk[j] * row[j] * __expf(gi - ms.gam[j]) : 0.f;
-            ms.cq[i] = __expf(gi) * fqi;
+            const float gt = ms.gam[tid], last = ms.gam[kC - 1];
+            const float eg = __expf(gt);
+            ms.wk[tid] = ms.bet[tid] * eg * ms.fk[tid];
+            ms.rr[tid] = __expf(last - gt) * ms.fk[tid];
+            ms.cq[tid] = eg * ms.fq[tid];
         }
-        __syncthreads();
-        // (6) A = (I + L)^-1.
-        unit_lower_inverse_64(Lf, X, Tm, tid);
-        // (7) The two column scalings of A, as bf16 K-major B operands.
         {
-            const int i = tid & 63;
-            const float* Xrow = X + i * kC;
-            float a[kC];
-            if (tid < kC) {
+            const bool key_row = qd < 2;
+            const int i = key_row ? row : row - kC;
+            const float gli = ms.gl[i];
+            const float rowf = key_row ? ms.bet[i] * ms.fk[i] : ms.fq[i];
+            const int lim = key_row ? i : i + 1;  // j < lim survives
+            float v[32];
 #pragma unroll
-                for (int j = 0; j < kC; ++j) a[j] = Xrow[j] * ms.bet[j];
-            } else {
-#pragma unroll
-                for (int j = 0; j < kC; ++j) a[j] = Xrow[j] * ms.wk[j];
+            for (int jj = 0; jj < 32; ++jj) {
+                const int j = 32 * hf + jj;
+                const float e = ex2(gli - ms.gl[j]);
+                v[jj] = (j < lim) ? rowf * (ms.fk[j] * gr[jj]) * e : 0.f;
             }
-            store_row_sw128(AB + (tid < kC ? 0 : kTileBytes), i, a);
+            if (key_row) {
+                float4* dst = reinterpret_cast<float4*>(Lf + i * kLd + 32 * hf);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            } else {
+                store_half_row_sw128(IN, i, 4 * hf, v);
+            }
+        }
+        __syncthreads();
+        // (g) A = (I + L)^-1.
+        unit_lower_inverse_64(Lf, X, reinterpret_cast<float*>(AB), tid);
+        // (h) The two column scalings of A, as bf16 K-major B operands.
+        {
+            const int mtx = tid >> 7, hh = (tid >> 6) & 1, i = tid & 63;
+            const float* fac = mtx ? ms.wk : ms.bet;
+            const float4* src = reinterpret_cast<const float4*>(X + i * kLd + 32 * hh);
+            float a[32];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float4 x = src[c];
+                a[4 * c + 0] = x.x * fac[32 * hh + 4 * c + 0];
+                a[4 * c + 1] = x.y * fac[32 * hh + 4 * c + 1];
+                a[4 * c + 2] = x.z * fac[32 * hh + 4 * c + 2];
+                a[4 * c + 3] = x.w * fac[32 * hh + 4 * c + 3];
+            }
+            store_half_row_sw128(AB + mtx * kTileBytes, i, 4 * hh, a);
         }
         fence_proxy_async();
         __syncthreads();
-        // (8) G2: U^T = V^T Au^T -> R1; W^T = K^T Aw^T -> R0.
+        // (i) G2: U^T = V^T Au^T -> R1; W^T = K^T Aw^T -> R0.
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 1, 0, 0);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tbase + kColR1, sdesc_sw128(sVB + ks * 2048, 8192, 1024),
                           sdesc_sw128(sAB + ks * 32, 16, 1024), id, ks > 0);
-            }
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tbase + kColR0, sdesc_sw128(sKQ + ks * 2048, 16384, 1024),
                           sdesc_sw128(sAB + kTileBytes + ks * 32, 16, 1024), id, ks > 0);
-            }
             umma_commit(&ms.bar_mma);
+        }
+        // (j) While G2 runs: S^T -> bf16 operand; S^T <- e^gamma_C S^T.
+        {
+            const float decay = __expf(ms.gam[kC - 1]);
+#pragma unroll 1
+            for (int cb = 0; cb < 2; ++cb) {
+                float x[32];
+                const uint32_t col = kColS + 64 * hf + 32 * cb;
+                tmem_ld32(lane_addr + col, x);
+                tmem_wait_ld();
+                store_half_row_sw128(ST + hf * 16384, row, 4 * cb, x);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[i] *= decay;
+                tmem_st32(lane_addr + col, x);
+            }
+            tmem_wait_st();
         }
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
-        // (9) S^T -> bf16 operand (ST), S^T <- e^gamma_C S^T; W^T -> bf16 (VB);
-        //     intra rows -> bf16 (AB, over the consumed A diag(beta)).
+        // (l) W^T -> bf16 MN-major operand (over V, which G2 consumed).
         {
-            const int d = tid;
-            const float decay = __expf(ms.gam[kC - 1]);
-#pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-                float x[64];
-                float a[32], b[32];
-                tmem_ld32(tS + half * 64, a);
-                tmem_ld32(tS + half * 64 + 32, b);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    x[i] = a[i];
-                    x[32 + i] = b[i];
-                }
-                store_row_sw128(ST + half * 16384, d, x);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    a[i] *= decay;
-                    b[i] *= decay;
-                }
-                tmem_st32(tS + half * 64, a);
-                tmem_st32(tS + half * 64 + 32, b);
-            }
-            float w[64];
-            {
-                float a[32], b[32];
-                tmem_ld32(tR0, a);
-                tmem_ld32(tR0 + 32, b);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    w[i] = a[i];
-                    w[32 + i] = b[i];
-                }
-            }
-            store_row_sw128(VB, d, w);
-            if (tid >= kC) store_row_sw128(AB, tid - kC, row);
-            tmem_wait_st();
+            float w[32];
+            tmem_ld32(lane_addr + kColR0 + 32 * hf, w);
+            tmem_wait_ld();
+            store_half_row_sw128(VB, row, 4 * hf, w);
         }
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
-        // (10) G3: R1 += -(S^T W^T); R0 = S^T Q^T.
+        // (m) G3: R1 += -(S^T W^T); R0 = S^T Q^T.
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id_w = idesc_bf16(128, 64, 0, 1, 1);
@@ -457,69 +499,57 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
         }
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
-        // (11) V_new^T -> bf16 operands: plain (ST) and scaled by rr (ST + 16K).
+        // (n) V_new^T -> bf16 operands: plain (ST) and scaled by rr (ST + 16K).
         {
-            const int d = tid;
-            float vn[64];
-            {
-                float a[32], b[32];
-                tmem_ld32(tR1, a);
-                tmem_ld32(tR1 + 32, b);
-                tmem_wait_ld();
+            float vn[32];
+            tmem_ld32(lane_addr + kColR1 + 32 * hf, vn);
+            tmem_wait_ld();
+            store_half_row_sw128(ST, row, 4 * hf, vn);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    vn[i] = a[i];
-                    vn[32 + i] = b[i];
-                }
-            }
-            store_row_sw128(ST, d, vn);
-#pragma unroll
-            for (int t = 0; t < kC; ++t) vn[t] *= ms.rr[t];
-            store_row_sw128(ST + 16384, d, vn);
+            for (int t = 0; t < 32; ++t) vn[t] *= ms.rr[32 * hf + t];
+            store_half_row_sw128(ST + 16384, row, 4 * hf, vn);
         }
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
-        // (12) G4: R1 = V_new^T intra^T; G5: S^T += (V_new^T o rr) K.
+        // (o) G4: R1 = V_new^T intra^T; G5: S^T += (V_new^T o rr) K.
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id4 = idesc_bf16(128, 64, 0, 0, 0);
             const uint32_t id5 = idesc_bf16(128, 128, 0, 1, 0);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tbase + kColR1, sdesc_sw128(sST + ks * 32, 16, 1024),
-                          sdesc_sw128(sAB + ks * 32, 16, 1024), id4, ks > 0);
-            }
+                          sdesc_sw128(sIN + ks * 32, 16, 1024), id4, ks > 0);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
+            for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tbase + kColS, sdesc_sw128(sST + 16384 + ks * 32, 16, 1024),
                           sdesc_sw128(sKQ + ks * 2048, 16384, 1024), id5, 1);
-            }
             umma_commit(&ms.bar_mma);
         }
+        // (p) The next chunk's gates, into registers.
+        if (tid < kC && ci + 1 < n_chunks) load_gates(ci + 1, pg, pb);
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
-        // (13) O^T = (Q S)^T diag(cq) + (intra V_new)^T -> bf16 staging [t][d].
+        // (r) The next chunk's tiles load while this chunk's output is written.
+        if (tid == 0 && ci + 1 < n_chunks) issue_tiles(ci + 1);
+        // (s) O^T = (Q S)^T diag(cq) + (intra V_new)^T -> bf16 staging [t][d].
         {
-            const int d = tid;
             float qs[32], iv[32];
-            __nv_bfloat16* OS = reinterpret_cast<__nv_bfloat16*>(VB);
-#pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-                tmem_ld32(tR0 + half * 32, qs);
-                tmem_ld32(tR1 + half * 32, iv);
-                tmem_wait_ld();
+            tmem_ld32(lane_addr + kColR0 + 32 * hf, qs);
+            tmem_ld32(lane_addr + kColR1 + 32 * hf, iv);
+            tmem_wait_ld();
+            __nv_bfloat16* OS = reinterpret_cast<__nv_bfloat16*>(ST);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int t = half * 32 + i;
-                    OS[t * kD + d] = __float2bfloat16_rn(fmaf(qs[i], ms.cq[t], iv[i]));
-                }
+            for (int i = 0; i < 32; ++i) {
+                const int t = 32 * hf + i;
+                OS[t * kD + row] = __float2bfloat16_rn(fmaf(qs[i], ms.cq[t], iv[i]));
             }
         }
         tc_fence_before();
         __syncthreads();
         {
-            const uint4* src = reinterpret_cast<const uint4*>(VB);
+            const uint4* src = reinterpret_cast<const uint4*>(ST);
             for (int e = tid; e < valid * 16; e += kThreads) {
                 const int t = e >> 4, c = e & 15;
                 uint4* dst = reinterpret_cast<uint4*>(out + ((tok0 + t) * p.heads_v + h) * kD) + c;
@@ -532,15 +562,15 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 
     // The final state, S^T lane d -> S[:, d].
     if (ok) {
-        const int d = tid;
         tc_fence_after();
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int cb = 0; cb < 2; ++cb) {
             float x[32];
-            tmem_ld32(tS + cb * 32, x);
+            const int c0 = 64 * hf + 32 * cb;
+            tmem_ld32(lane_addr + kColS + c0, x);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) state_out[head_state + (cb * 32 + i) * kD + d] = x[i];
+            for (int i = 0; i < 32; ++i) state_out[head_state + (c0 + i) * kD + row] = x[i];
         }
     } else if (tid == 0) {
         // Give in-flight copies and MMAs a last bounded chance to land before

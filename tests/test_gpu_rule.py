@@ -230,3 +230,21 @@ def test_empty_batch_is_a_no_op():
                                        x["beta"][:0], None, cu_seqlens=x["cu_seqlens"])
     torch.cuda.synchronize()
     assert out.shape == (0, 4, 128) and st.shape == (0, 4, 128, 128)
+
+
+def test_zero_length_sequences_pass_the_state_through():
+    """Sequences with no tokens return their state unchanged (zeros without
+    one), on every path."""
+    x = _rand_bf16([3], state=True)
+    cu = torch.zeros(3, dtype=torch.int32, device=DEV)
+    s0 = torch.randn(2, 4, 128, 128, device=DEV)
+    e = {k: x[k][:0] for k in ("q", "k", "v", "g", "beta")}
+    for form in ("chunked", "recurrent"):
+        out, st = getattr(GatedDeltaRule(), form)(e["q"], e["k"], e["v"], e["g"], e["beta"], s0,
+                                                  cu_seqlens=cu)
+        torch.cuda.synchronize()
+        assert out.shape == (0, 4, 128) and torch.equal(st, s0)
+        _, st = getattr(GatedDeltaRule(), form)(e["q"], e["k"], e["v"], e["g"], e["beta"], None,
+                                                cu_seqlens=cu)
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(st) == 0
