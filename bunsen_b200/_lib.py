@@ -44,8 +44,8 @@ SIGNATURES = {
     "gdr_recurrent": (_i32, _RULE_ARGS),
     "gdr_chunked": (_i32, _RULE_ARGS),
     "gdr_mixed_workspace_size": (_sz, [ctypes.POINTER(GdrParams)]),
-    "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
-                         _vp, _sz, _vp]),
+    "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
+                         _vp, _vp, _vp, _sz, _vp]),
     "gdr_device_error": (_i32, []),
     "gdr_status_string": (ctypes.c_char_p, [_i32]),
     "gdr_abi_version": (_i32, []),

@@ -18,6 +18,10 @@ cudaError_t launch_chunked_tc(const Problem&, const void*, const void*, const vo
                               const float*, const float*, const float*, void*, float*,
                               cudaStream_t);
 cudaError_t take_device_error(int* flag);
+size_t mixed_workspace_bytes(int n_seqs);
+cudaError_t launch_mixed_tc(const Problem&, const void*, const void*, const void*, const float*,
+                            const float*, float*, const int32_t*, int32_t, void*, int32_t*,
+                            cudaStream_t);
 }  // namespace gdr
 
 namespace {
@@ -117,24 +121,37 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
 }
 
 size_t gdr_mixed_workspace_size(const gdr_params* params) {
-    (void)params;
-    return 0;
+    if (params == nullptr || params->n_seqs < 0) return 0;
+    return gdr::mixed_workspace_bytes(params->n_seqs);
 }
 
 gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, const void* v,
                      const float* g, const float* beta, float* state_pool,
-                     const int32_t* state_slots, void* out, const int32_t* cu_seqlens,
-                     void* workspace, size_t workspace_bytes, void* stream) {
-    (void)params, (void)q, (void)k, (void)v, (void)g, (void)beta, (void)state_pool;
-    (void)state_slots, (void)out, (void)cu_seqlens, (void)workspace, (void)workspace_bytes;
-    (void)stream;
-    return GDR_ERR_UNSUPPORTED;
+                     const int32_t* state_slots, int32_t n_slots, void* out,
+                     const int32_t* cu_seqlens, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+    if (cu_seqlens == nullptr) return GDR_ERR_INVALID;
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    if (params->chunk_size <= 0) return GDR_ERR_INVALID;
+    if (!io_ok(p, q, k, v, g, beta, out, state_pool)) return GDR_ERR_INVALID;
+    if (p.n_seqs > 0 && n_slots <= 0) return GDR_ERR_INVALID;
+    if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 3) != 0 ||
+        workspace_bytes < gdr::mixed_workspace_bytes(p.n_seqs))
+        return GDR_ERR_INVALID;
+    if (!gdr::chunked_tc_supports(*params)) return GDR_ERR_UNSUPPORTED;
+    if (p.n_seqs == 0 || total_tokens(p) == 0) return GDR_OK;
+    return from_cuda(gdr::launch_mixed_tc(p, q, k, v, g, beta, state_pool, state_slots, n_slots,
+                                          out, static_cast<int32_t*>(workspace),
+                                          static_cast<cudaStream_t>(stream)));
 }
 
 gdr_status gdr_device_error(void) {
     int flag = 0;
     if (gdr::take_device_error(&flag) != cudaSuccess) return GDR_ERR_CUDA;
-    return flag ? GDR_ERR_TIMEOUT : GDR_OK;
+    if (flag & 1) return GDR_ERR_TIMEOUT;
+    return (flag & 2) ? GDR_ERR_INVALID : GDR_OK;
 }
 
 const char* gdr_status_string(gdr_status status) {

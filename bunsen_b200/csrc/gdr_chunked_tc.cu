@@ -48,11 +48,14 @@
 #include <cudaTypedefs.h>
 
 #include "gdr_common.cuh"
+#include "gdr_decode.cuh"
 #include "gdr_sm100.cuh"
 
 namespace gdr {
 
-__device__ int g_tc_error;  // set when a bounded wait in the kernel ran out
+// Device-side failures since the last gdr_device_error: bit 0, a bounded wait
+// ran out; bit 1, a state slot outside the pool.
+__device__ int g_tc_error;
 
 namespace {
 
@@ -72,6 +75,7 @@ constexpr uint32_t kOffX = kC * kLd * 4;  // A after L inside ST
 constexpr uint32_t kTileBytes = 8192;     // one 64 x 64 bf16 TMA box
 constexpr uint32_t kSmemBytes = kOffMisc + 3072 + 1024;  // + alignment slack
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kOsStride = 160;  // bf16 row stride of the output staging tile
 
 struct Misc {
     float gam[kC];  // cumulative log decay within the chunk
@@ -170,11 +174,14 @@ __device__ __forceinline__ void store16(float* M, int ld, const float (&c)[2][4]
 }
 
 // A = (I + L)^-1 for the strictly lower 64 x 64 L in `Lf` into `X` (both f32,
-// row stride kLd; X zero above the diagonal). The 16 x 16 diagonal blocks by
-// exact forward substitution; then the blocks below, one diagonal at a time,
-// X_ij = -X_ii sum_{k=j}^{i-1} L_ik X_kj, with tf32 mma.sync. `Tm` holds 16 x
-// 24 f32 of scratch per warp for 3 warps.
-__device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Tm, int tid) {
+// row stride kLd; X zero above the diagonal), with 16 x 16 blocks:
+//  D  the diagonal blocks X_ii = (I + L_ii)^-1 by exact forward substitution;
+//  N  N_ij = X_ii L_ij for the six blocks below the diagonal (tf32 mma.sync);
+//  then X_ij = -sum_{k=j}^{i-1} N_ik X_kj, one block diagonal per level, each
+//  product issued as soon as its X_kj exists, so three levels of one product
+//  each follow N. `Nm` holds the six N blocks (16 x 20 f32 each).
+constexpr int kLdN = 20;
+__device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Nm, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     if (tid < 64) {
         const int b = tid >> 4, m = tid & 15;
@@ -188,44 +195,64 @@ __device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Tm, int 
             for (int r = s + 1; r < 16; ++r) x[r] = fmaf(-Lb[r * kLd + s], x[s], x[r]);
 #pragma unroll
         for (int r = 0; r < 16; ++r) X[(16 * b + r) * kLd + 16 * b + m] = x[r];
-    } else {
-        // The six blocks above the block diagonal are zero.
-        for (int e = tid - 64; e < 6 * 256; e += kThreads - 64) {
-            const int blk = e >> 8, r = (e >> 4) & 15, c = e & 15;
-            const int ib = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-            const int jb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-            X[(16 * ib + r) * kLd + 16 * jb + c] = 0.f;
+    } else if (tid < 128) {
+        // Blocks (0, 1) and (2, 3) above the diagonal are read as zeros (the
+        // rest of the upper triangle is never read).
+        for (int e = tid - 64; e < 2 * 256; e += 64) {
+            const int ib = (e >> 8) * 2, r = (e >> 4) & 15, c = e & 15;
+            X[(16 * ib + r) * kLd + 16 * (ib + 1) + c] = 0.f;
         }
     }
     __syncthreads();
-#pragma unroll 1
-    for (int lvl = 1; lvl < 4; ++lvl) {
-        if (warp < 4 - lvl) {
-            const int jb = warp, ib = jb + lvl;
-            float* T = Tm + warp * 16 * 24;
-            float c[2][4] = {};
-#pragma unroll 1
-            for (int kb = jb; kb < ib; ++kb)
-                mma16_tf32(Lf + (16 * ib) * kLd + 16 * kb, kLd, X + (16 * kb) * kLd + 16 * jb, kLd,
-                           c, lane);
-            store16(T, 24, c, 1.f, lane);
-            __syncwarp();
-            float d[2][4] = {};
-            mma16_tf32(X + (16 * ib) * kLd + 16 * ib, kLd, T, 24, d, lane);
-            store16(X + (16 * ib) * kLd + 16 * jb, kLd, d, -1.f, lane);
-        }
-        __syncthreads();
+    // Block pairs (i, j) of N, by warp: (1,0) (2,1) (3,2) (2,0) (3,1) (3,0).
+    const int pi = warp < 3 ? warp + 1 : (warp < 5 ? warp - 1 : 3);
+    const int pj = warp < 3 ? warp : (warp < 5 ? warp - 3 : 0);
+    auto Xb = [&](int i, int j) { return X + (16 * i) * kLd + 16 * j; };
+    auto Nb = [&](int w) { return Nm + w * 16 * kLdN; };
+    if (warp < 6) {
+        float c[2][4] = {};
+        mma16_tf32(Xb(pi, pi), kLd, Lf + (16 * pi) * kLd + 16 * pj, kLd, c, lane);
+        store16(Nb(warp), kLdN, c, 1.f, lane);
     }
+    __syncthreads();
+    float c[2][4] = {};
+    // Level 1: X_10, X_21, X_32; and the parts of X_20, X_31, X_30 that only
+    // need diagonal blocks.
+    if (warp < 6) {
+        mma16_tf32(Nb(warp), kLdN, Xb(pj, pj), kLd, c, lane);  // N_ij X_jj
+        if (warp < 3) store16(Xb(pi, pj), kLd, c, -1.f, lane);
+    }
+    __syncthreads();
+    // Level 2: X_20 += N_21 X_10, X_31 += N_32 X_21; X_30 gathers N_31 X_10.
+    if (warp == 3) {
+        mma16_tf32(Nb(1), kLdN, Xb(1, 0), kLd, c, lane);
+        store16(Xb(2, 0), kLd, c, -1.f, lane);
+    } else if (warp == 4) {
+        mma16_tf32(Nb(2), kLdN, Xb(2, 1), kLd, c, lane);
+        store16(Xb(3, 1), kLd, c, -1.f, lane);
+    } else if (warp == 5) {
+        mma16_tf32(Nb(4), kLdN, Xb(1, 0), kLd, c, lane);
+    }
+    __syncthreads();
+    // Level 3: X_30 += N_32 X_20.
+    if (warp == 5) {
+        mma16_tf32(Nb(2), kLdN, Xb(2, 0), kLd, c, lane);
+        store16(Xb(3, 0), kLd, c, -1.f, lane);
+    }
+    __syncthreads();
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
-chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
-           const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-           const float* __restrict__ g, const float* __restrict__ beta, const float* state_in,
-           __nv_bfloat16* __restrict__ out, float* state_out) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+// One (sequence, value head): positions [t0, t0 + len) of value head h, from
+// state_in (null: zeros; may equal state_out) to state_out, both that head's
+// [d_k, d_v] f32 state. `smem` is the CTA's 1024-aligned dynamic shared
+// memory. Allocates and frees 256 TMEM columns.
+__device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap* tm_q,
+                                             const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                                             const float* __restrict__ g,
+                                             const float* __restrict__ beta,
+                                             __nv_bfloat16* __restrict__ out, int64_t t0,
+                                             int64_t len, int h, const float* state_in,
+                                             float* state_out, uint8_t* smem) {
     uint8_t* KQ = smem + kOffKQ;
     uint8_t* VB = smem + kOffVB;
     uint8_t* AB = smem + kOffAB;
@@ -238,11 +265,7 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int qd = warp & 3, hf = warp >> 2;
     const int row = 32 * qd + lane;  // this thread's TMEM lane
-    const int h = blockIdx.x, s = blockIdx.y;
     const int hq = h / p.group;
-    int64_t t0, t1;
-    seq_span(p, s, t0, t1);
-    const int64_t len = t1 - t0;
     const int n_chunks = static_cast<int>((len + kC - 1) / kC);
 
     if (tid == 0) {
@@ -260,44 +283,72 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     const uint32_t tbase = ms.tmem_base;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(qd * 32) << 16);
-    const uint32_t sKQ = smem_u32(KQ), sVB = smem_u32(VB), sAB = smem_u32(AB);
-    const uint32_t sIN = smem_u32(IN), sST = smem_u32(ST);
+    // Operand descriptors; a tile offset is added to the start-address field.
+    const uint64_t dKQ = sdesc_sw128(smem_u32(KQ), 16, 1024);      // K-major K, Q
+    const uint64_t dKQmn = sdesc_sw128(smem_u32(KQ), 16384, 1024);  // MN-major K
+    const uint64_t dVBmn = sdesc_sw128(smem_u32(VB), 8192, 1024);   // MN-major V, W^T
+    const uint64_t dAB = sdesc_sw128(smem_u32(AB), 16, 1024);
+    const uint64_t dIN = sdesc_sw128(smem_u32(IN), 16, 1024);
+    const uint64_t dST = sdesc_sw128(smem_u32(ST), 16, 1024);
+    auto at = [](uint64_t d, uint32_t off) { return d + (off >> 4); };
 
     auto issue_tiles = [&](int ci) {  // thread 0: chunk ci's K, Q, V tiles
         fence_proxy_async();
         mbar_expect_tx(&ms.bar_tma, 6 * kTileBytes);
         const int tok = static_cast<int>(t0 + static_cast<int64_t>(ci) * kC);
-        tma_load_3d(KQ + 0 * kTileBytes, &tm_k, &ms.bar_tma, 0, hq, tok);
-        tma_load_3d(KQ + 1 * kTileBytes, &tm_q, &ms.bar_tma, 0, hq, tok);
-        tma_load_3d(KQ + 2 * kTileBytes, &tm_k, &ms.bar_tma, 64, hq, tok);
-        tma_load_3d(KQ + 3 * kTileBytes, &tm_q, &ms.bar_tma, 64, hq, tok);
-        tma_load_3d(VB + 0 * kTileBytes, &tm_v, &ms.bar_tma, 0, h, tok);
-        tma_load_3d(VB + 1 * kTileBytes, &tm_v, &ms.bar_tma, 64, h, tok);
+        tma_load_3d(KQ + 0 * kTileBytes, tm_k, &ms.bar_tma, 0, hq, tok);
+        tma_load_3d(KQ + 1 * kTileBytes, tm_q, &ms.bar_tma, 0, hq, tok);
+        tma_load_3d(KQ + 2 * kTileBytes, tm_k, &ms.bar_tma, 64, hq, tok);
+        tma_load_3d(KQ + 3 * kTileBytes, tm_q, &ms.bar_tma, 64, hq, tok);
+        tma_load_3d(VB + 0 * kTileBytes, tm_v, &ms.bar_tma, 0, h, tok);
+        tma_load_3d(VB + 1 * kTileBytes, tm_v, &ms.bar_tma, 64, h, tok);
         if (ci + 1 < n_chunks) {
             const int nt = tok + kC;
-            tma_prefetch_3d(&tm_k, 0, hq, nt);
-            tma_prefetch_3d(&tm_k, 64, hq, nt);
-            tma_prefetch_3d(&tm_q, 0, hq, nt);
-            tma_prefetch_3d(&tm_q, 64, hq, nt);
-            tma_prefetch_3d(&tm_v, 0, h, nt);
-            tma_prefetch_3d(&tm_v, 64, h, nt);
+            tma_prefetch_3d(tm_k, 0, hq, nt);
+            tma_prefetch_3d(tm_k, 64, hq, nt);
+            tma_prefetch_3d(tm_q, 0, hq, nt);
+            tma_prefetch_3d(tm_q, 64, hq, nt);
+            tma_prefetch_3d(tm_v, 0, h, nt);
+            tma_prefetch_3d(tm_v, 64, h, nt);
         }
     };
-    // The gates of chunk ci, zero past the end (tid < 64).
-    auto load_gates = [&](int ci, float& pg, float& pb) {
-        const int64_t pos = static_cast<int64_t>(ci) * kC + tid;
-        const bool in = pos < len;
-        const int64_t gi = (t0 + pos) * p.heads_v + h;
-        pg = in ? g[gi] : 0.f;
-        pb = in ? beta[gi] : 0.f;
+    // Warp 0: chunk ci's gates (positions 2 lane, 2 lane + 1; zero past the
+    // end) into registers ...
+    auto load_gates = [&](int ci, float (&pg)[2], float (&pb)[2]) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int64_t pos = static_cast<int64_t>(ci) * kC + 2 * lane + u;
+            const bool in = pos < len;
+            const int64_t gi = (t0 + pos) * p.heads_v + h;
+            pg[u] = in ? g[gi] : 0.f;
+            pb[u] = in ? beta[gi] : 0.f;
+        }
+    };
+    // ... then into shared memory, the log decay as its running sum.
+    auto put_gates = [&](const float (&pg)[2], const float (&pb)[2]) {
+        float incl = pg[0] + pg[1];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const float g0 = incl - pg[1], g1 = incl;
+        ms.gam[2 * lane] = g0;
+        ms.gam[2 * lane + 1] = g1;
+        ms.gl[2 * lane] = g0 * kLog2e;
+        ms.gl[2 * lane + 1] = g1 * kLog2e;
+        ms.bet[2 * lane] = pb[0];
+        ms.bet[2 * lane + 1] = pb[1];
     };
 
     if (tid == 0 && n_chunks > 0) issue_tiles(0);
-    float pg = 0.f, pb = 0.f;
-    if (tid < kC && n_chunks > 0) load_gates(0, pg, pb);
+    float pg[2] = {0.f, 0.f}, pb[2] = {0.f, 0.f};
+    if (warp == 0 && n_chunks > 0) {
+        load_gates(0, pg, pb);
+        put_gates(pg, pb);
+    }
 
     // The initial state, transposed into TMEM: lane d holds S[:, d].
-    const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
     {
 #pragma unroll 1
         for (int cb = 0; cb < 2; ++cb) {
@@ -305,7 +356,7 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             const int c0 = 64 * hf + 32 * cb;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                x[i] = state_in ? state_in[head_state + (c0 + i) * kD + row] : 0.f;
+                x[i] = state_in ? state_in[(c0 + i) * kD + row] : 0.f;
             tmem_st32(lane_addr + kColS + c0, x);
         }
         tmem_wait_st();
@@ -318,7 +369,7 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     auto wait = [&](uint64_t* bar, uint32_t& ph) {
         if (!mbar_wait(bar, ph, kWaitLimitNs)) {
             ms.failed = 1;
-            atomicExch(&g_tc_error, 1);
+            atomicOr(&g_tc_error, 1);
         }
         ph ^= 1u;
     };
@@ -328,27 +379,8 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
         const int64_t tok0 = t0 + static_cast<int64_t>(ci) * kC;
         const int64_t left = len - static_cast<int64_t>(ci) * kC;
         const int valid = static_cast<int>(left < kC ? left : kC);
-        // (a) Gates; the cumulative decay by a warp scan.
-        if (tid < kC) {
-            ms.gam[tid] = pg;
-            ms.bet[tid] = pb;
-        }
-        __syncthreads();
-        if (warp == 0) {
-            const float a = ms.gam[2 * lane], b = ms.gam[2 * lane + 1];
-            float incl = a + b;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            const float excl = incl - (a + b);
-            ms.gam[2 * lane] = excl + a;
-            ms.gam[2 * lane + 1] = excl + a + b;
-            ms.gl[2 * lane] = (excl + a) * kLog2e;
-            ms.gl[2 * lane + 1] = (excl + a + b) * kLog2e;
-        }
-        // (b)+(c) The tiles, then G1: [K;Q] [K;Q]^T -> G.
+        // (b)+(c) The tiles (this chunk's gates are in shared memory), then
+        //       G1: [K;Q] [K;Q]^T -> G.
         wait(&ms.bar_tma, ph_tma);
         if (tid == 0) {
             tc_fence_after();
@@ -356,8 +388,7 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColG, sdesc_sw128(sKQ + off, 16, 1024),
-                          sdesc_sw128(sKQ + off, 16, 1024), id, ks > 0);
+                umma_bf16(tbase + kColG, at(dKQ, off), at(dKQ, off), id, ks > 0);
             }
             umma_commit(&ms.bar_mma);
         }
@@ -385,6 +416,7 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
         tc_fence_before();
         __syncthreads();
         // (f) Per-position factors; rows of L (f32) and of intra (bf16 operand).
+        const float decay = __expf(ms.gam[kC - 1]);
         if (tid < kC) {
             const float gt = ms.gam[tid], last = ms.gam[kC - 1];
             const float eg = __expf(gt);
@@ -395,15 +427,34 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
         {
             const bool key_row = qd < 2;
             const int i = key_row ? row : row - kC;
-            const float gli = ms.gl[i];
-            const float rowf = key_row ? ms.bet[i] * ms.fk[i] : ms.fq[i];
-            const int lim = key_row ? i : i + 1;  // j < lim survives
+            // This warp's 32 x 32 block of rows (i) and columns (j): below the
+            // diagonal, on it, or above it (all zero) -- uniform per warp.
+            const int rblk = key_row ? qd : qd - 2;
             float v[32];
+            if (rblk < hf) {
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                const int j = 32 * hf + jj;
-                const float e = ex2(gli - ms.gl[j]);
-                v[jj] = (j < lim) ? rowf * (ms.fk[j] * gr[jj]) * e : 0.f;
+                for (int jj = 0; jj < 32; ++jj) v[jj] = 0.f;
+            } else {
+                const float gli = ms.gl[i];
+                const float rowf = key_row ? ms.bet[i] * ms.fk[i] : ms.fq[i];
+                const int lim = key_row ? i : i + 1;  // j < lim survives
+                const float4* gl4 = reinterpret_cast<const float4*>(ms.gl + 32 * hf);
+                const float4* fk4 = reinterpret_cast<const float4*>(ms.fk + 32 * hf);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 gl = gl4[c], fk = fk4[c];
+                    const float glv[4] = {gl.x, gl.y, gl.z, gl.w};
+                    const float fkv[4] = {fk.x, fk.y, fk.z, fk.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int jj = 4 * c + u;
+                        v[jj] = rowf * (fkv[u] * gr[jj]) * ex2(gli - glv[u]);
+                    }
+                }
+                if (rblk == hf) {
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) v[jj] = (32 * hf + jj < lim) ? v[jj] : 0.f;
+                }
             }
             if (key_row) {
                 float4* dst = reinterpret_cast<float4*>(Lf + i * kLd + 32 * hf);
@@ -422,14 +473,20 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             const int mtx = tid >> 7, hh = (tid >> 6) & 1, i = tid & 63;
             const float* fac = mtx ? ms.wk : ms.bet;
             const float4* src = reinterpret_cast<const float4*>(X + i * kLd + 32 * hh);
+            const float4* f4 = reinterpret_cast<const float4*>(fac + 32 * hh);
             float a[32];
+            if (32 * hh > i) {  // above the diagonal: uniform per warp
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float4 x = src[c];
-                a[4 * c + 0] = x.x * fac[32 * hh + 4 * c + 0];
-                a[4 * c + 1] = x.y * fac[32 * hh + 4 * c + 1];
-                a[4 * c + 2] = x.z * fac[32 * hh + 4 * c + 2];
-                a[4 * c + 3] = x.w * fac[32 * hh + 4 * c + 3];
+                for (int c = 0; c < 32; ++c) a[c] = 0.f;
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 x = src[c], f = f4[c];
+                    a[4 * c + 0] = x.x * f.x;
+                    a[4 * c + 1] = x.y * f.y;
+                    a[4 * c + 2] = x.z * f.z;
+                    a[4 * c + 3] = x.w * f.w;
+                }
             }
             store_half_row_sw128(AB + mtx * kTileBytes, i, 4 * hh, a);
         }
@@ -441,17 +498,15 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             const uint32_t id = idesc_bf16(128, 64, 1, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColR1, sdesc_sw128(sVB + ks * 2048, 8192, 1024),
-                          sdesc_sw128(sAB + ks * 32, 16, 1024), id, ks > 0);
+                umma_bf16(tbase + kColR1, at(dVBmn, ks * 2048), at(dAB, ks * 32), id, ks > 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColR0, sdesc_sw128(sKQ + ks * 2048, 16384, 1024),
-                          sdesc_sw128(sAB + kTileBytes + ks * 32, 16, 1024), id, ks > 0);
+                umma_bf16(tbase + kColR0, at(dKQmn, ks * 2048), at(dAB, kTileBytes + ks * 32),
+                          id, ks > 0);
             umma_commit(&ms.bar_mma);
         }
         // (j) While G2 runs: S^T -> bf16 operand; S^T <- e^gamma_C S^T.
         {
-            const float decay = __expf(ms.gam[kC - 1]);
 #pragma unroll 1
             for (int cb = 0; cb < 2; ++cb) {
                 float x[32];
@@ -485,15 +540,13 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColR1, sdesc_sw128(sST + aoff, 16, 1024),
-                          sdesc_sw128(sVB + ks * 2048, 8192, 1024), id_w, 1);
+                umma_bf16(tbase + kColR1, at(dST, aoff), at(dVBmn, ks * 2048), id_w, 1);
             }
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
                 const uint32_t boff = kTileBytes + (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColR0, sdesc_sw128(sST + aoff, 16, 1024),
-                          sdesc_sw128(sKQ + boff, 16, 1024), id_q, ks > 0);
+                umma_bf16(tbase + kColR0, at(dST, aoff), at(dKQ, boff), id_q, ks > 0);
             }
             umma_commit(&ms.bar_mma);
         }
@@ -505,8 +558,15 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             tmem_ld32(lane_addr + kColR1 + 32 * hf, vn);
             tmem_wait_ld();
             store_half_row_sw128(ST, row, 4 * hf, vn);
+            const float4* rr4 = reinterpret_cast<const float4*>(ms.rr + 32 * hf);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) vn[t] *= ms.rr[32 * hf + t];
+            for (int c = 0; c < 8; ++c) {
+                const float4 r = rr4[c];
+                vn[4 * c] *= r.x;
+                vn[4 * c + 1] *= r.y;
+                vn[4 * c + 2] *= r.z;
+                vn[4 * c + 3] *= r.w;
+            }
             store_half_row_sw128(ST + 16384, row, 4 * hf, vn);
         }
         tc_fence_before();
@@ -519,16 +579,17 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             const uint32_t id5 = idesc_bf16(128, 128, 0, 1, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColR1, sdesc_sw128(sST + ks * 32, 16, 1024),
-                          sdesc_sw128(sIN + ks * 32, 16, 1024), id4, ks > 0);
+                umma_bf16(tbase + kColR1, at(dST, ks * 32), at(dIN, ks * 32), id4, ks > 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColS, sdesc_sw128(sST + 16384 + ks * 32, 16, 1024),
-                          sdesc_sw128(sKQ + ks * 2048, 16384, 1024), id5, 1);
+                umma_bf16(tbase + kColS, at(dST, 16384 + ks * 32), at(dKQmn, ks * 2048), id5, 1);
             umma_commit(&ms.bar_mma);
         }
-        // (p) The next chunk's gates, into registers.
-        if (tid < kC && ci + 1 < n_chunks) load_gates(ci + 1, pg, pb);
+        // (p) The next chunk's gates (this chunk's are no longer read).
+        if (warp == 0 && ci + 1 < n_chunks) {
+            load_gates(ci + 1, pg, pb);
+            put_gates(pg, pb);
+        }
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
         // (r) The next chunk's tiles load while this chunk's output is written.
@@ -539,21 +600,39 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             tmem_ld32(lane_addr + kColR0 + 32 * hf, qs);
             tmem_ld32(lane_addr + kColR1 + 32 * hf, iv);
             tmem_wait_ld();
-            __nv_bfloat16* OS = reinterpret_cast<__nv_bfloat16*>(ST);
+            const float4* cq4 = reinterpret_cast<const float4*>(ms.cq + 32 * hf);
+            float o[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int t = 32 * hf + i;
-                OS[t * kD + row] = __float2bfloat16_rn(fmaf(qs[i], ms.cq[t], iv[i]));
+            for (int c = 0; c < 8; ++c) {
+                const float4 q = cq4[c];
+                o[4 * c] = fmaf(qs[4 * c], q.x, iv[4 * c]);
+                o[4 * c + 1] = fmaf(qs[4 * c + 1], q.y, iv[4 * c + 1]);
+                o[4 * c + 2] = fmaf(qs[4 * c + 2], q.z, iv[4 * c + 2]);
+                o[4 * c + 3] = fmaf(qs[4 * c + 3], q.w, iv[4 * c + 3]);
+            }
+            // Lanes 2m and 2m+1 hold features d, d+1 of every position: swap
+            // so that the even lane stores (t, d..d+1) for even t and the odd
+            // lane for odd t, as 32-bit words of the [t][d] staging tile.
+            uint32_t* OS = reinterpret_cast<uint32_t*>(ST);
+            const bool odd = lane & 1;
+            const int d0 = row & ~1;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                const float send = odd ? o[i] : o[i + 1];
+                const float got = __shfl_xor_sync(0xffffffffu, send, 1);
+                const int t = 32 * hf + i + (odd ? 1 : 0);
+                const uint32_t w = odd ? pack_bf16(got, o[i + 1]) : pack_bf16(o[i], got);
+                OS[t * (kOsStride / 2) + (d0 >> 1)] = w;
             }
         }
         tc_fence_before();
         __syncthreads();
         {
-            const uint4* src = reinterpret_cast<const uint4*>(ST);
             for (int e = tid; e < valid * 16; e += kThreads) {
                 const int t = e >> 4, c = e & 15;
+                const uint4* src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2) + c;
                 uint4* dst = reinterpret_cast<uint4*>(out + ((tok0 + t) * p.heads_v + h) * kD) + c;
-                *dst = src[e];
+                *dst = *src;
             }
         }
         __syncthreads();
@@ -570,7 +649,7 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             tmem_ld32(lane_addr + kColS + c0, x);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) state_out[head_state + (c0 + i) * kD + row] = x[i];
+            for (int i = 0; i < 32; ++i) state_out[(c0 + i) * kD + row] = x[i];
         }
     } else if (tid == 0) {
         // Give in-flight copies and MMAs a last bounded chance to land before
@@ -581,6 +660,139 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tbase, kTmemCols);
+}
+
+__device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
+                                      ~static_cast<uintptr_t>(1023));
+}
+
+// Packs of at most this many sequences run longest first.
+constexpr int kRankMax = 128;
+
+// The sequence of rank y when a packed batch's sequences are ordered by
+// length, longest first (ties by index). Every thread gets the answer.
+__device__ int longest_first(const Problem& p, int y, uint8_t* scratch) {
+    int* lens = reinterpret_cast<int*>(scratch);
+    int* pick = lens + kRankMax;
+    const int n = p.n_seqs;
+    for (int s = threadIdx.x; s < n; s += blockDim.x) {
+        int64_t a, b;
+        seq_span(p, s, a, b);
+        lens[s] = static_cast<int>(b - a);
+    }
+    if (threadIdx.x == 0) *pick = y;
+    __syncthreads();
+    for (int s = threadIdx.x; s < n; s += blockDim.x) {
+        const int ls = lens[s];
+        int rank = 0;
+        for (int u = 0; u < n; ++u) rank += (lens[u] > ls) || (lens[u] == ls && u < s);
+        if (rank == y) *pick = s;
+    }
+    __syncthreads();
+    const int s = *pick;
+    __syncthreads();
+    return s;
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
+           const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+           const float* __restrict__ g, const float* __restrict__ beta, const float* state_in,
+           __nv_bfloat16* __restrict__ out, float* state_out) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = aligned_smem(smem_raw);
+    const int h = blockIdx.x, y = blockIdx.y;
+    const int s = (p.cu_seqlens != nullptr && p.n_seqs <= kRankMax)
+                      ? longest_first(p, y, smem + kOffST)
+                      : y;
+    int64_t t0, t1;
+    seq_span(p, s, t0, t1);
+    const int64_t hs = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
+    prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, h,
+                 state_in ? state_in + hs : nullptr, state_out + hs, smem);
+}
+
+// The work list of a continuous batch, built in the caller's workspace:
+// work[0] = prefill sequences (length > 1), work[1] = decode rows (length 1),
+// then the sequence indices, prefill ones first by decreasing chunk count,
+// then the decode rows. One CTA of 1024 threads; sequences of length 0 are
+// left out.
+constexpr int kPlanBuckets = 1024;
+__global__ void __launch_bounds__(1024)
+plan_mixed(const Problem p, int32_t* work) {
+    __shared__ int hist[kPlanBuckets];
+    __shared__ int n_pre, n_dec;
+    const int n = p.n_seqs;
+    auto bucket = [&](int64_t len) {  // descending chunk count
+        const int64_t c = (len + kC - 1) / kC;
+        return kPlanBuckets - 1 - static_cast<int>(c < kPlanBuckets - 1 ? c : kPlanBuckets - 1);
+    };
+    for (int i = threadIdx.x; i < kPlanBuckets; i += blockDim.x) hist[i] = 0;
+    if (threadIdx.x == 0) n_pre = n_dec = 0;
+    __syncthreads();
+    for (int s = threadIdx.x; s < n; s += blockDim.x) {
+        int64_t a, b;
+        seq_span(p, s, a, b);
+        if (b - a > 1) {
+            atomicAdd(&hist[bucket(b - a)], 1);
+            atomicAdd(&n_pre, 1);
+        } else if (b - a == 1) {
+            atomicAdd(&n_dec, 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // exclusive scan of the buckets into cursors
+        int acc = 0;
+        for (int i = 0; i < kPlanBuckets; ++i) {
+            const int c = hist[i];
+            hist[i] = acc;
+            acc += c;
+        }
+        work[0] = n_pre;
+        work[1] = n_dec;
+        n_dec = n_pre;  // cursor of the decode rows
+    }
+    __syncthreads();
+    for (int s = threadIdx.x; s < n; s += blockDim.x) {
+        int64_t a, b;
+        seq_span(p, s, a, b);
+        if (b - a > 1)
+            work[2 + atomicAdd(&hist[bucket(b - a)], 1)] = s;
+        else if (b - a == 1)
+            work[2 + atomicAdd(&n_dec, 1)] = s;
+    }
+}
+
+// A continuous batch: CTA row y < work[0] runs prefill sequence work[2 + y]
+// through prefill_item; the next work[1] rows run one decode row each through
+// the CUDA-core recurrent body. States live in place in `pool` at the
+// sequence's slot (slots null: the sequence index).
+__global__ void __launch_bounds__(kThreads, 2)
+mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
+         const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+         const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+         const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
+         const float* __restrict__ beta, float* pool, const int32_t* slots, int32_t n_slots,
+         __nv_bfloat16* __restrict__ out, const int32_t* work) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = aligned_smem(smem_raw);
+    const int h = blockIdx.x, y = blockIdx.y;
+    const int n_pre = work[0], n_dec = work[1];
+    if (y >= n_pre + n_dec) return;
+    const int s = work[2 + y];
+    const int slot = slots ? slots[s] : s;
+    if (slot < 0 || slot >= n_slots) {
+        if (threadIdx.x == 0) atomicOr(&g_tc_error, 2);
+        return;
+    }
+    float* st = pool + (static_cast<int64_t>(slot) * p.heads_v + h) * kD * kD;
+    int64_t t0, t1;
+    seq_span(p, s, t0, t1);
+    if (y < n_pre)
+        prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, h, st, st, smem);
+    else
+        recurrent_d128_item<__nv_bfloat16>(p, q, k, v, g, beta, t0, t1, h, st, out, st, smem);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -626,27 +838,53 @@ bool chunked_tc_supports(const gdr_params& a) {
     return a.dtype == GDR_DTYPE_BF16 && a.d_k == kD && a.d_v == kD && a.chunk_size == kC;
 }
 
-cudaError_t launch_chunked_tc(const Problem& p, const void* q, const void* k, const void* v,
-                              const float* g, const float* beta, const float* state_in, void* out,
-                              float* state_out, cudaStream_t stream) {
+static cudaError_t make_maps(const Problem& p, const void* q, const void* k, const void* v,
+                             const void* out, CUtensorMap* mq, CUtensorMap* mk, CUtensorMap* mv) {
     const uintptr_t align = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                             reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
     if (align & 15) return cudaErrorMisalignedAddress;
     const int64_t tokens = p.cu_seqlens ? p.seq_len : static_cast<int64_t>(p.n_seqs) * p.seq_len;
     if (tokens >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
-    CUtensorMap mq, mk, mv;
-    if (!make_map(&mq, q, tokens, p.heads_qk) || !make_map(&mk, k, tokens, p.heads_qk) ||
-        !make_map(&mv, v, tokens, p.heads_v))
+    if (!make_map(mq, q, tokens, p.heads_qk) || !make_map(mk, k, tokens, p.heads_qk) ||
+        !make_map(mv, v, tokens, p.heads_v))
         return cudaErrorInvalidValue;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(chunked_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    return cudaSuccess;
+}
+
+template <typename K>
+static cudaError_t allow_smem(K* kernel) {
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kSmemBytes));
+}
+
+cudaError_t launch_chunked_tc(const Problem& p, const void* q, const void* k, const void* v,
+                              const float* g, const float* beta, const float* state_in, void* out,
+                              float* state_out, cudaStream_t stream) {
+    CUtensorMap mq, mk, mv;
+    cudaError_t e = make_maps(p, q, k, v, out, &mq, &mk, &mv);
+    if (e != cudaSuccess) return e;
+    if ((e = allow_smem(chunked_tc)) != cudaSuccess) return e;
     chunked_tc<<<dim3(p.heads_v, p.n_seqs), kThreads, kSmemBytes, stream>>>(
         p, mq, mk, mv, g, beta, state_in, static_cast<__nv_bfloat16*>(out), state_out);
+    return cudaGetLastError();
+}
+
+size_t mixed_workspace_bytes(int n_seqs) {
+    return (static_cast<size_t>(n_seqs) + 2) * sizeof(int32_t);
+}
+
+cudaError_t launch_mixed_tc(const Problem& p, const void* q, const void* k, const void* v,
+                            const float* g, const float* beta, float* pool, const int32_t* slots,
+                            int32_t n_slots, void* out, int32_t* work, cudaStream_t stream) {
+    CUtensorMap mq, mk, mv;
+    cudaError_t e = make_maps(p, q, k, v, out, &mq, &mk, &mv);
+    if (e != cudaSuccess) return e;
+    if ((e = allow_smem(mixed_tc)) != cudaSuccess) return e;
+    plan_mixed<<<1, 1024, 0, stream>>>(p, work);
+    mixed_tc<<<dim3(p.heads_v, p.n_seqs), kThreads, kSmemBytes, stream>>>(
+        p, mq, mk, mv, static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+        static_cast<const __nv_bfloat16*>(v), g, beta, pool, slots, n_slots,
+        static_cast<__nv_bfloat16*>(out), work);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,138 @@
+// The d_k = d_v = 128 recurrent rule for one (sequence, value head), as a
+// device function of a 256-thread CTA: the body of gdr_recurrent's fast
+// kernel and of gdr_mixed's decode rows.
+//
+// GatedDeltaRule::recurrent (delta_rule.rs:182-209) per position t:
+//   S <- exp(g_t) S;  read = k_t^T S;  delta = (v_t - read) beta_t;
+//   S <- S + k_t delta^T;  o_t = q_t^T S
+// Bandwidth bound: the f32 state is read from HBM once and written once (64
+// KiB each way). Warp w holds state rows w, w+8, ..., w+120 and lane l
+// columns 4l..4l+3 in registers, so every state access is a 128-bit load or
+// store and a warp touches one whole 512-byte row per instruction. The two
+// reductions over d_k (k^T S and q^T S) share one pass: o = q^T S_decayed +
+// delta (q . k), which is q^T S after the rank-one update.
+#pragma once
+
+#include "gdr_common.cuh"
+
+namespace gdr {
+
+constexpr int kDecD = 128;
+constexpr int kDecWarps = 8;
+constexpr int kDecRowsPerWarp = kDecD / kDecWarps;  // 16 state rows per thread
+
+struct DecodeSmem {
+    float qk_raw[2][kDecD];            // this position's q and k
+    float red[2][kDecWarps][kDecD];    // per-warp partial k^T S, q^T S
+    float delta_s[kDecD];
+    float scal[4];                     // |q|^2, |k|^2, -, q.k
+};
+
+// Positions [t0, t1) of value head h; state_in may be null (zeros) and may
+// equal state_out. `smem` holds a DecodeSmem.
+template <typename T>
+__device__ __forceinline__ void recurrent_d128_item(const Problem& p, const T* __restrict__ q,
+                                                    const T* __restrict__ k,
+                                                    const T* __restrict__ v,
+                                                    const float* __restrict__ g,
+                                                    const float* __restrict__ beta,
+                                                    int64_t t0, int64_t t1, int h,
+                                                    const float* state_in, T* __restrict__ out,
+                                                    float* state_out, uint8_t* smem) {
+    constexpr int kD = kDecD, kWarps = kDecWarps, kRowsPerWarp = kDecRowsPerWarp;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    auto& sh = *reinterpret_cast<DecodeSmem*>(smem);
+    auto& qk_raw = sh.qk_raw;
+    auto& red = sh.red;
+    auto& delta_s = sh.delta_s;
+    auto& scal = sh.scal;
+    const int col = 4 * lane;
+    float st[kRowsPerWarp][4];
+    if (state_in != nullptr) {
+        const float* src = state_in;
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const float4 x =
+                *reinterpret_cast<const float4*>(src + (warp + kWarps * r) * kD + col);
+            st[r][0] = x.x; st[r][1] = x.y; st[r][2] = x.z; st[r][3] = x.w;
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) st[r][0] = st[r][1] = st[r][2] = st[r][3] = 0.f;
+    }
+
+    const int hq = h / p.group;
+    for (int64_t t = t0; t < t1; ++t) {
+        // q and k of this position, raw, into shared memory.
+        const int64_t qk_off = (t * p.heads_qk + hq) * kD;
+        qk_raw[tid >> 7][tid & 127] = to_f32(((tid < 128) ? q : k)[qk_off + (tid & 127)]);
+        const int64_t gate = t * p.heads_v + h;
+        const float decay = __expf(g[gate]);
+        const float bt = beta[gate];
+        __syncthreads();
+        if (warp < 3) {  // |q|^2, |k|^2, q.k
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a[i] = qk_raw[warp == 1 ? 1 : 0][col + i];
+                b[i] = qk_raw[warp == 0 ? 0 : 1][col + i];
+            }
+            float acc = a[0] * b[0] + a[1] * b[1] + a[2] * b[2] + a[3] * b[3];
+            acc = warp_sum(acc);
+            if (lane == 0) scal[warp == 2 ? 3 : warp] = acc;  // 0: |q|^2 1: |k|^2 3: q.k
+        }
+        __syncthreads();
+        const float fq = l2_factor(p, scal[0]) * p.q_scale;
+        const float fk = l2_factor(p, scal[1]);
+        float pk[4] = {0.f, 0.f, 0.f, 0.f}, pq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const int row = warp + kWarps * r;
+            const float kr = qk_raw[1][row] * fk, qr = qk_raw[0][row] * fq;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                st[r][c] *= decay;
+                pk[c] = fmaf(kr, st[r][c], pk[c]);
+                pq[c] = fmaf(qr, st[r][c], pq[c]);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            red[0][warp][col + c] = pk[c];
+            red[1][warp][col + c] = pq[c];
+        }
+        __syncthreads();
+        if (tid < kD) {
+            float read = 0.f, qs = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                read += red[0][w][tid];
+                qs += red[1][w][tid];
+            }
+            const float vj = to_f32(v[(t * p.heads_v + h) * kD + tid]);
+            const float d = (vj - read) * bt;
+            delta_s[tid] = d;
+            const float qk_dot = scal[3] * fq * fk;
+            out[(t * p.heads_v + h) * kD + tid] = from_f32<T>(fmaf(d, qk_dot, qs));
+        }
+        __syncthreads();
+        float dl[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) dl[c] = delta_s[col + c];
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const float kr = qk_raw[1][warp + kWarps * r] * fk;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) st[r][c] = fmaf(kr, dl[c], st[r][c]);
+        }
+        __syncthreads();  // qk_raw, red and delta_s are rewritten next position
+    }
+
+    float* dst = state_out;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r)
+        *reinterpret_cast<float4*>(dst + (warp + kWarps * r) * kD + col) =
+            make_float4(st[r][0], st[r][1], st[r][2], st[r][3]);
+}
+
+}  // namespace gdr

@@ -18,14 +18,11 @@
 //    one thread per column. For small or unusual head sizes (bunsen's unit
 //    test shapes); not a performance path.
 #include "gdr_common.cuh"
+#include "gdr_decode.cuh"
 
 namespace gdr {
 
 namespace {
-
-constexpr int kD = 128;         // d_k = d_v of the fast path
-constexpr int kWarps = 8;       // warps per CTA
-constexpr int kRowsPerWarp = kD / kWarps;  // 16 state rows per thread
 
 template <typename T>
 __global__ void __launch_bounds__(256, 2)
@@ -33,104 +30,13 @@ recurrent_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
                const T* __restrict__ v, const float* __restrict__ g,
                const float* __restrict__ beta, const float* state_in, T* __restrict__ out,
                float* state_out) {
+    __shared__ __align__(16) uint8_t smem[sizeof(DecodeSmem)];
     const int h = blockIdx.x, s = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int64_t t0, t1;
     seq_span(p, s, t0, t1);
-
-    __shared__ float qk_raw[2][kD];          // this position's q and k
-    __shared__ float red[2][kWarps][kD];     // per-warp partial k^T S, q^T S
-    __shared__ float delta_s[kD];
-    __shared__ float scal[4];                // q factor, k factor, q.k
-
-    const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
-    const int col = 4 * lane;
-    float st[kRowsPerWarp][4];
-    if (state_in != nullptr) {
-        const float* src = state_in + head_state;
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) {
-            const float4 x =
-                *reinterpret_cast<const float4*>(src + (warp + kWarps * r) * kD + col);
-            st[r][0] = x.x; st[r][1] = x.y; st[r][2] = x.z; st[r][3] = x.w;
-        }
-    } else {
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) st[r][0] = st[r][1] = st[r][2] = st[r][3] = 0.f;
-    }
-
-    const int hq = h / p.group;
-    for (int64_t t = t0; t < t1; ++t) {
-        // q and k of this position, raw, into shared memory.
-        const int64_t qk_off = (t * p.heads_qk + hq) * kD;
-        qk_raw[tid >> 7][tid & 127] = to_f32(((tid < 128) ? q : k)[qk_off + (tid & 127)]);
-        const int64_t gate = t * p.heads_v + h;
-        const float decay = __expf(g[gate]);
-        const float bt = beta[gate];
-        __syncthreads();
-        if (warp < 3) {  // |q|^2, |k|^2, q.k
-            float a[4], b[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a[i] = qk_raw[warp == 1 ? 1 : 0][col + i];
-                b[i] = qk_raw[warp == 0 ? 0 : 1][col + i];
-            }
-            float acc = a[0] * b[0] + a[1] * b[1] + a[2] * b[2] + a[3] * b[3];
-            acc = warp_sum(acc);
-            if (lane == 0) scal[warp == 2 ? 3 : warp] = acc;  // 0: |q|^2 1: |k|^2 3: q.k
-        }
-        __syncthreads();
-        const float fq = l2_factor(p, scal[0]) * p.q_scale;
-        const float fk = l2_factor(p, scal[1]);
-        float pk[4] = {0.f, 0.f, 0.f, 0.f}, pq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) {
-            const int row = warp + kWarps * r;
-            const float kr = qk_raw[1][row] * fk, qr = qk_raw[0][row] * fq;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                st[r][c] *= decay;
-                pk[c] = fmaf(kr, st[r][c], pk[c]);
-                pq[c] = fmaf(qr, st[r][c], pq[c]);
-            }
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            red[0][warp][col + c] = pk[c];
-            red[1][warp][col + c] = pq[c];
-        }
-        __syncthreads();
-        if (tid < kD) {
-            float read = 0.f, qs = 0.f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                read += red[0][w][tid];
-                qs += red[1][w][tid];
-            }
-            const float vj = to_f32(v[(t * p.heads_v + h) * kD + tid]);
-            const float d = (vj - read) * bt;
-            delta_s[tid] = d;
-            const float qk_dot = scal[3] * fq * fk;
-            out[(t * p.heads_v + h) * kD + tid] = from_f32<T>(fmaf(d, qk_dot, qs));
-        }
-        __syncthreads();
-        float dl[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) dl[c] = delta_s[col + c];
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) {
-            const float kr = qk_raw[1][warp + kWarps * r] * fk;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) st[r][c] = fmaf(kr, dl[c], st[r][c]);
-        }
-        __syncthreads();  // qk_raw, red and delta_s are rewritten next position
-    }
-
-    float* dst = state_out + head_state;
-#pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r)
-        *reinterpret_cast<float4*>(dst + (warp + kWarps * r) * kD + col) =
-            make_float4(st[r][0], st[r][1], st[r][2], st[r][3]);
+    const int64_t hs = (static_cast<int64_t>(s) * p.heads_v + h) * kDecD * kDecD;
+    recurrent_d128_item<T>(p, q, k, v, g, beta, t0, t1, h, state_in ? state_in + hs : nullptr,
+                           out, state_out + hs, smem);
 }
 
 // Any d_k, d_v <= 256. Shared memory: the state (d_k * d_v f32), q and k.
@@ -198,7 +104,7 @@ static cudaError_t launch_recurrent_t(const Problem& p, const void* q, const voi
                                       const float* state_in, void* out, float* state_out,
                                       cudaStream_t stream) {
     const dim3 grid(p.heads_v, p.n_seqs);
-    if (p.d_k == kD && p.d_v == kD) {
+    if (p.d_k == kDecD && p.d_v == kDecD) {
         recurrent_d128<T><<<grid, 256, 0, stream>>>(
             p, static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
             beta, state_in, static_cast<T*>(out), state_out);

@@ -40,12 +40,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// As mbar_try_wait, but the thread may sleep up to `hint_ns` for the phase
+// instead of returning at once, so waiting threads issue no instructions.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 // Waits for the phase with this parity to complete, for at most `limit_ns`
 // of wall time; false when the limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     const uint64_t start = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity))
+    while (!mbar_try_wait_sleep(bar, parity, 100000u))
         if (globaltimer_ns() - start > limit_ns) return false;
     return true;
 }

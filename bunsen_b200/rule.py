@@ -64,6 +64,43 @@ class GatedDeltaRule:
         assert self.chunk_size > 0, "a chunk of at least one position"
         return self._run("gdr_chunked", q, k, v, g, beta, state, cu_seqlens, out, state_out)
 
+    def mixed(self, q, k, v, g, beta, state_pool, *, cu_seqlens, state_slots=None, out=None,
+              workspace=None):
+        """A continuous batch in one launch (``gdr_mixed``): the packed batch's
+        length-1 sequences step as decode rows (``recurrent``), longer ones run
+        as prefill segments (``chunked``). Sequence ``s`` updates its state in
+        place at ``state_pool[state_slots[s]]``. Returns ``out``."""
+        assert self.chunk_size > 0, "a chunk of at least one position"
+        check_shapes(q, k, v, g, beta, None, cu_seqlens)
+        dev = q.device
+        if dev.type != "cuda":
+            raise RuntimeError("libgdr runs on CUDA tensors only")
+        if state_pool.dtype != torch.float32 or not state_pool.is_contiguous():
+            raise TypeError("the state pool is contiguous f32 [n_slots, H_v, d_k, d_v]")
+        h_v, d_k, d_v = v.shape[-2], q.shape[-1], v.shape[-1]
+        if tuple(state_pool.shape[1:]) != (h_v, d_k, d_v):
+            raise ValueError(f"the state pool is [n_slots, {h_v}, {d_k}, {d_v}]")
+        g = g.to(torch.float32).contiguous()
+        beta = beta.to(torch.float32).contiguous()
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        cu_seqlens = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+        if state_slots is not None:
+            state_slots = state_slots.to(device=dev, dtype=torch.int32).contiguous()
+        if out is None:
+            out = torch.empty(v.shape, dtype=q.dtype, device=dev)
+        p = self.params(q, v, cu_seqlens)
+        lib = _lib.load()
+        need = lib.gdr_mixed_workspace_size(ctypes.byref(p))
+        if workspace is None:
+            workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=dev)
+        status = lib.gdr_mixed(
+            ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
+            beta.data_ptr(), state_pool.data_ptr(), _ptr(state_slots), state_pool.shape[0],
+            out.data_ptr(), cu_seqlens.data_ptr(), workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), _stream(dev))
+        _lib.check("gdr_mixed", status)
+        return out
+
     # -- plumbing ------------------------------------------------------------
     def params(self, q, v, cu_seqlens) -> _lib.GdrParams:
         if cu_seqlens is None:

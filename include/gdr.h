@@ -116,22 +116,30 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
 
 /* A continuous batch in one launch: the packed batch of `cu_seqlens`, whose
  * sequences of length 1 are decode rows (run as gdr_recurrent would) and whose
- * longer sequences are prefill segments (run as gdr_chunked would). Sequence s
- * reads and writes its state in place at `state_pool[state_slots[s]]`
- * ([n_slots, H_v, d_k, d_v] f32); `state_slots` NULL means slot s. A slot
- * holds its sequence's state on entry (a fresh sequence's slot holds zeros).
- * Work is scheduled longest-first from a device-side work list that the call
- * builds in `workspace` (device memory of at least
- * gdr_mixed_workspace_size(params) bytes, owned by the caller). */
+ * longer sequences are prefill segments (run as gdr_chunked would); sequences
+ * of length 0 are left alone. Sequence s reads and writes its state in place
+ * at `state_pool[state_slots[s]]` ([n_slots, H_v, d_k, d_v] f32);
+ * `state_slots` NULL means slot s. A slot holds its sequence's state on entry
+ * (a fresh sequence's slot holds zeros); two sequences of one call must not
+ * share a slot. A slot outside [0, n_slots) skips its sequence and is
+ * reported by gdr_device_error as GDR_ERR_INVALID.
+ * Work runs from a device-side work list -- prefill segments first, longest
+ * first, then decode rows -- that the call builds in `workspace`: device
+ * memory of at least gdr_mixed_workspace_size(params) bytes, 4-byte aligned,
+ * owned by the caller; calls that overlap on the GPU need separate
+ * workspaces. Kernel family: bf16, d_k = d_v = 128, chunk 64
+ * (GDR_ERR_UNSUPPORTED otherwise); `out` as for gdr_chunked. */
 size_t gdr_mixed_workspace_size(const gdr_params* params);
 gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, const void* v,
                      const float* g, const float* beta, float* state_pool,
-                     const int32_t* state_slots, void* out, const int32_t* cu_seqlens,
-                     void* workspace, size_t workspace_bytes, void* stream);
+                     const int32_t* state_slots, int32_t n_slots, void* out,
+                     const int32_t* cu_seqlens, void* workspace, size_t workspace_bytes,
+                     void* stream);
 
-/* GDR_ERR_TIMEOUT if a kernel of this library gave up a bounded device-side
- * wait since the last call (and clears the record), else GDR_OK.
- * Synchronous: waits for the device's outstanding work. */
+/* What the kernels of this library recorded on the device since the last
+ * call (the record is then cleared): GDR_ERR_TIMEOUT if one gave up a bounded
+ * wait, else GDR_ERR_INVALID if gdr_mixed met a state slot outside its pool,
+ * else GDR_OK. Synchronous: waits for the device's outstanding work. */
 gdr_status gdr_device_error(void);
 
 /* A short English description of a status. */
