@@ -13,6 +13,8 @@ PKG = pathlib.Path(__file__).resolve().parent
 LIB_PATH = PKG / "libgdr.so"
 
 GDR_OK, GDR_ERR_INVALID, GDR_ERR_UNSUPPORTED, GDR_ERR_CUDA, GDR_ERR_TIMEOUT = range(5)
+GDR_ERR_CAPACITY = 5
+GDR_MIXED_NOALLOC_MAX_SEQS = 16384
 GDR_DTYPE_F32, GDR_DTYPE_BF16 = 0, 1
 GDR_ALGO_AUTO, GDR_ALGO_CUDA_CORE, GDR_ALGO_TENSOR = 0, 1, 2
 
@@ -46,6 +48,8 @@ SIGNATURES = {
     "gdr_mixed_workspace_size": (_sz, [ctypes.POINTER(GdrParams)]),
     "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                          _vp, _vp, _vp, _sz, _vp]),
+    "gdr_mixed_noalloc": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _i32, _vp, _vp, _vp]),
     "gdr_device_error": (_i32, []),
     "gdr_status_string": (ctypes.c_char_p, [_i32]),
     "gdr_abi_version": (_i32, []),

@@ -18,6 +18,10 @@ cudaError_t launch_chunked_tc(const Problem&, const void*, const void*, const vo
                               const float*, const float*, const float*, void*, float*,
                               cudaStream_t);
 cudaError_t take_device_error(int* flag);
+int mixed_noalloc_max_seqs();
+cudaError_t launch_mixed_tc_noalloc(const Problem&, const void*, const void*, const void*,
+                                    const float*, const float*, float*, const int32_t*, int32_t,
+                                    void*, cudaStream_t);
 size_t mixed_workspace_bytes(int n_seqs);
 cudaError_t launch_mixed_tc(const Problem&, const void*, const void*, const void*, const float*,
                             const float*, float*, const int32_t*, int32_t, void*, int32_t*,
@@ -147,6 +151,24 @@ gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, con
                                           static_cast<cudaStream_t>(stream)));
 }
 
+gdr_status gdr_mixed_noalloc(const gdr_params* params, const void* q, const void* k,
+                             const void* v, const float* g, const float* beta, float* state_pool,
+                             const int32_t* state_slots, int32_t n_slots, void* out,
+                             const int32_t* cu_seqlens, void* stream) {
+    if (cu_seqlens == nullptr) return GDR_ERR_INVALID;
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    if (params->chunk_size <= 0) return GDR_ERR_INVALID;
+    if (!io_ok(p, q, k, v, g, beta, out, state_pool)) return GDR_ERR_INVALID;
+    if (p.n_seqs > 0 && n_slots <= 0) return GDR_ERR_INVALID;
+    if (p.n_seqs > gdr::mixed_noalloc_max_seqs()) return GDR_ERR_CAPACITY;
+    if (!gdr::chunked_tc_supports(*params)) return GDR_ERR_UNSUPPORTED;
+    if (p.n_seqs == 0 || total_tokens(p) == 0) return GDR_OK;
+    return from_cuda(gdr::launch_mixed_tc_noalloc(p, q, k, v, g, beta, state_pool, state_slots,
+                                                  n_slots, out, static_cast<cudaStream_t>(stream)));
+}
+
 gdr_status gdr_device_error(void) {
     int flag = 0;
     if (gdr::take_device_error(&flag) != cudaSuccess) return GDR_ERR_CUDA;
@@ -161,6 +183,9 @@ const char* gdr_status_string(gdr_status status) {
         case GDR_ERR_UNSUPPORTED: return "no kernel for these dimensions or dtypes";
         case GDR_ERR_CUDA: return "a CUDA call or launch failed";
         case GDR_ERR_TIMEOUT: return "a bounded device-side wait ran out";
+        case GDR_ERR_CAPACITY:
+            return "more sequences than gdr_mixed_noalloc's fixed work list holds "
+                   "(GDR_MIXED_NOALLOC_MAX_SEQS)";
     }
     return "unknown status";
 }

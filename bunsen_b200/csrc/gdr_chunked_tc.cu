@@ -47,6 +47,8 @@
 //               staging
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "gdr_common.cuh"
 #include "gdr_decode.cuh"
 #include "gdr_sm100.cuh"
@@ -886,6 +888,51 @@ cudaError_t launch_mixed_tc(const Problem& p, const void* q, const void* k, cons
         static_cast<const __nv_bfloat16*>(v), g, beta, pool, slots, n_slots,
         static_cast<__nv_bfloat16*>(out), work);
     return cudaGetLastError();
+}
+
+// ---- gdr_mixed without a caller workspace ----------------------------------
+// The work list of gdr_mixed_noalloc lives in this fixed device array instead
+// of caller-provided memory: 2 counters plus one entry per sequence, for at
+// most kMixedNoAllocMaxSeqs sequences (64 KiB). Every GPU that loads the
+// library holds one copy until the process exits. All calls on a device share
+// it and it keeps the previous call's contents; the planning kernel rewrites
+// every entry a call reads, so nothing needs clearing, but calls whose work
+// overlaps on the GPU (different streams, no ordering between them) race on
+// it.
+constexpr int kMixedNoAllocMaxSeqs = GDR_MIXED_NOALLOC_MAX_SEQS;
+static __device__ __align__(256) int32_t g_mixed_scratch[2 + kMixedNoAllocMaxSeqs];
+
+// The device address of g_mixed_scratch on the current device, looked up once
+// per device (host code cannot use the symbol itself as a device pointer).
+static cudaError_t mixed_scratch_ptr(int32_t** out) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static int32_t* ptrs[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (ptrs[dev] == nullptr) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_mixed_scratch);
+        if (e != cudaSuccess) return e;
+        ptrs[dev] = static_cast<int32_t*>(ptr);
+    }
+    *out = ptrs[dev];
+    return cudaSuccess;
+}
+
+int mixed_noalloc_max_seqs() { return kMixedNoAllocMaxSeqs; }
+
+cudaError_t launch_mixed_tc_noalloc(const Problem& p, const void* q, const void* k,
+                                    const void* v, const float* g, const float* beta,
+                                    float* pool, const int32_t* slots, int32_t n_slots,
+                                    void* out, cudaStream_t stream) {
+    int32_t* work = nullptr;
+    cudaError_t e = mixed_scratch_ptr(&work);
+    if (e != cudaSuccess) return e;
+    return launch_mixed_tc(p, q, k, v, g, beta, pool, slots, n_slots, out, work, stream);
 }
 
 }  // namespace gdr

@@ -69,7 +69,8 @@ typedef enum gdr_status {
     GDR_ERR_INVALID = 1,     /* bad shape, pointer or option (bunsen: panic) */
     GDR_ERR_UNSUPPORTED = 2, /* valid, but no kernel for these dims/dtypes   */
     GDR_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed         */
-    GDR_ERR_TIMEOUT = 4      /* a bounded device-side wait ran out           */
+    GDR_ERR_TIMEOUT = 4,     /* a bounded device-side wait ran out           */
+    GDR_ERR_CAPACITY = 5     /* more than a fixed-size entry point can take  */
 } gdr_status;
 
 typedef enum gdr_dtype {
@@ -135,6 +136,30 @@ gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, con
                      const int32_t* state_slots, int32_t n_slots, void* out,
                      const int32_t* cu_seqlens, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/* gdr_mixed for callers that cannot allocate device memory. No counterpart in
+ * the reference: bunsen allocates through burn on every call.
+ *
+ * Some callers may not allocate at all: a serving loop whose device memory
+ * is budgeted up front, code running under another framework's memory pool,
+ * or a host thread that must not take the allocator's locks or the device
+ * synchronisation a cudaMalloc/cudaFree can imply. This entry point takes the
+ * same arguments as gdr_mixed minus the workspace and allocates nothing: its
+ * work list lives in a fixed array inside the library, sized for at most
+ * GDR_MIXED_NOALLOC_MAX_SEQS sequences (64 KiB of device memory that every GPU
+ * loading the library holds until the process exits). A call with more
+ * sequences returns GDR_ERR_CAPACITY and launches nothing.
+ *
+ * The first call on each device looks the array's device address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture on
+ * that device. All calls on a device share the array: two calls whose work
+ * can overlap on the GPU (different streams with no ordering between them)
+ * race on it and must not be issued. */
+#define GDR_MIXED_NOALLOC_MAX_SEQS 16384
+gdr_status gdr_mixed_noalloc(const gdr_params* params, const void* q, const void* k,
+                             const void* v, const float* g, const float* beta, float* state_pool,
+                             const int32_t* state_slots, int32_t n_slots, void* out,
+                             const int32_t* cu_seqlens, void* stream);
 
 /* What the kernels of this library recorded on the device since the last
  * call (the record is then cleared): GDR_ERR_TIMEOUT if one gave up a bounded
