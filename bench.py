@@ -4,23 +4,29 @@
 One JSON line (rank 0). The headline `value` is ragged prefill tokens/s: one
 step is one gdr_chunked call over the whole ragged pack (131072 tokens in 64
 lognormal sequences, 16 q/k heads, 32 v heads, d 128, chunk 64, bf16, f32
-states), inputs resident in HBM (2.3 GB, larger than L2, so no flush is
-needed). The `decode` object carries the decode state-update figure: 64
-consecutive single-token steps over 256 rows with f32 states [256, 32, 128,
-128] updated in place.
+initial states), inputs resident in HBM (2.3 GB, larger than L2, so no flush
+is needed). Sub-objects carry the other workloads at the same N:
+  dense    8 x 4096 tokens, zero initial state (gdr_chunked)
+  decode   64 consecutive single-token steps over 256 rows, f32 states
+           [256, 32, 128, 128] updated in place (gdr_recurrent)
+  mixed    8 prefill segments x 2048 tokens + 1024 decode rows in one
+           gdr_mixed launch, states in place in a slot pool
+With N GPUs (torchrun), the key-head groups are sharded (rank r: key heads
+[16r/N, 16(r+1)/N) and their value heads) over the same tokens; no data
+crosses GPUs on the hot path; every time is the maximum over ranks; `value`
+counts the pack's tokens (all heads) once -- strong scaling. `--verify`
+gathers the sharded outputs (NCCL all_gather, outside the timed region) and
+compares them with an unsharded run on rank 0.
 
-With N GPUs (torchrun), the heads are sharded: rank r runs q/k heads
-[r*16/N, (r+1)*16/N) with their v heads over the same pack; no data crosses
-GPUs; the time is the maximum over ranks; `value` counts the pack's tokens
-(all heads) once -- strong scaling.
-
-`--impl reference` times the CPU oracle (a C++ restatement of bunsen's burn
-rule, OpenMP over all host threads) on a bounded sample of the same workload.
+`--impl reference` times the CPU oracle -- a C++ restatement of bunsen's burn
+rule (the reference itself is Rust and cannot be built here), OpenMP over all
+host threads -- on a bounded sample of the same ragged workload.
 """
 
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import pathlib
@@ -38,12 +44,13 @@ sys.path.insert(0, str(ROOT))
 
 from bunsen_b200 import _lib, workloads  # noqa: E402
 from bunsen_b200.rule import GatedDeltaRule  # noqa: E402
+from bunsen_b200.sharding import HeadShard  # noqa: E402
 
 METRIC = "GDR prefill tokens/sec (ragged) and decode state-update GB/s vs HBM peak"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
-# ---------------------------------------------------------------------------
+# -- roofline bookkeeping --------------------------------------------------------
 def peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -51,39 +58,53 @@ def peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def prefill_flops_per_token_head(c: int, d: int) -> float:
-    """Algorithmic FLOPs per token per v-head: 10 C d + 6 d^2 + (2/3) C^2 (the
-    chunk's matmuls: 5 C x C x d, 3 C x d x d, the C^3/3 inverse)."""
-    return 10 * c * d + 6 * d * d + (2.0 / 3.0) * c * c
+def prefill_flops(w: workloads.Workload, heads_v: int) -> float:
+    """Algorithmic FLOPs: per token per value head 10 C d + 6 d^2 + (2/3) C^2
+    (a chunk's five C x C x d and three C x d x d matmuls, and the C^3/3 of the
+    inverse)."""
+    c, d = w.chunk, w.d_k
+    return (10 * c * d + 6 * d * d + (2.0 / 3.0) * c * c) * w.tokens * heads_v
 
 
 def prefill_bytes(w: workloads.Workload, heads_qk: int, heads_v: int) -> float:
-    """Algorithmic HBM bytes of one prefill pass: q, k (once per q/k head),
-    v, out in bf16, g and beta in f32, states read (if given) and written."""
+    """Algorithmic HBM bytes: q, k once per key head, v and out in bf16, g and
+    beta in f32; states written, and read when the workload has them."""
     per_tok = heads_qk * w.d_k * 2 * 2 + heads_v * w.d_v * 2 * 2 + heads_v * 4 * 2
     states = w.n_seqs * heads_v * w.d_k * w.d_v * 4 * (2 if w.with_state else 1)
     return float(w.tokens * per_tok + states)
 
 
-def shard(x: dict, w: workloads.Workload, rank: int, world: int) -> dict:
-    """The q/k heads and v heads of rank `rank`."""
-    hq0, hq1 = rank * w.heads_qk // world, (rank + 1) * w.heads_qk // world
-    g = w.heads_v // w.heads_qk
-    out = {}
-    for k, t in x.items():
-        if k in ("q", "k"):
-            out[k] = t[..., hq0:hq1, :].contiguous()
-        elif k in ("v",):
-            out[k] = t[..., hq0 * g:hq1 * g, :].contiguous()
-        elif k in ("g", "beta"):
-            out[k] = t[..., hq0 * g:hq1 * g].contiguous()
-        elif k == "state":
-            out[k] = t[:, hq0 * g:hq1 * g].contiguous()
-        else:
-            out[k] = t
+def measured_traffic(tokens_heads: float) -> float | None:
+    """DRAM bytes of one prefill launch over `tokens_heads` token-heads, scaled
+    from the ncu capture recorded in profiles/traffic.json."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    rec = json.loads(p.read_text()).get("chunked_tc")
+    if not rec:
+        return None
+    return rec["dram_bytes"] / rec["token_heads"] * tokens_heads
+
+
+def roofline(flops: float, nbytes: float, kern_ms: float, pk: dict, pk_kind: str,
+             traffic: float | None) -> dict:
+    """The binding roof (sustained tensor or HBM) for this launch and the
+    fraction of it achieved."""
+    t_flop = flops / (pk["bf16_tflops_sustained"] * 1e12)
+    t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
+    s = kern_ms * 1e-3
+    if t_flop >= t_hbm:
+        out = {"bound": "tensor", "achieved": flops / s / 1e12, "peak": pk["bf16_tflops_sustained"],
+               "unit": "TFLOP/s"}
+    else:
+        out = {"bound": "hbm", "achieved": nbytes / s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
+    out["frac"] = out["achieved"] / out["peak"]
+    out.update(traffic=traffic, peak_source=pk_kind, flops_per_launch=flops,
+               bytes_per_launch=nbytes, tflops=flops / s / 1e12, gbs=nbytes / s / 1e9)
     return out
 
 
+# -- clocks, ranks, timing ---------------------------------------------------------
 class Clocks:
     """nvidia-smi samples during the timed region."""
 
@@ -100,10 +121,11 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            time.sleep(0.3)
         except FileNotFoundError:
             self.proc = None
         return self
@@ -124,9 +146,10 @@ class Clocks:
     def summary(self) -> dict:
         rows = [r for r in self.rows if len(r) >= 9]
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        num = lambda x: float(x) if x.replace(".", "").isdigit() else None  # noqa: E731
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
@@ -140,15 +163,12 @@ class Dist:
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
 
-    def init(self, backend: str = "nccl"):
+    def init(self):
         if self.world > 1:
-            import datetime
-
             import torch.distributed as dist
 
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local)
-                                    if backend == "nccl" else None)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
             self.pg = dist
         return self
 
@@ -170,8 +190,8 @@ class Dist:
 
 def timed(step, k: int, w: int, dist: Dist, stream) -> tuple[float, list[float]]:
     """W warm-up steps, then K timed steps bracketed by a barrier and a device
-    synchronize on both sides; per-step CUDA events on the launching stream.
-    Returns (max-over-ranks total ms, this rank's per-step ms)."""
+    synchronize on both sides; CUDA events on the launching stream around each
+    step. Returns (max-over-ranks total ms, this rank's per-step ms)."""
     for _ in range(w):
         step()
     torch.cuda.synchronize()
@@ -189,113 +209,126 @@ def timed(step, k: int, w: int, dist: Dist, stream) -> tuple[float, list[float]]
     return dist.max(evs[0].elapsed_time(evs[-1])), per
 
 
-# ---------------------------------------------------------------------------
-def cpu_sample_prefill(w: workloads.Workload, seconds_hint: float = 15.0) -> dict:
-    """The oracle's chunked form on a bounded sample of the ragged pack (the
-    first sequences, up to ~8k tokens, at 8 of the 32 v heads), all host
-    threads; tokens/s scaled to all heads."""
+# -- the CPU baseline -----------------------------------------------------------------
+def cpu_sample(w: workloads.Workload, max_tokens: int = 8192, heads_v: int = 8):
+    """A bounded sample of the ragged pack for the CPU oracle: its first
+    sequences up to `max_tokens` tokens, at `heads_v` of the value heads.
+    Returns (run, token-equivalents of the full-head workload, description)."""
     from oracle import oracle
 
     lens, tot = [], 0
     for L in w.seqlens:
-        if tot + L > 8192 and lens:
+        if tot + L > max_tokens and lens:
             break
         lens.append(L)
         tot += L
-    heads_v, heads_qk = 8, 4
+    heads_qk = heads_v * w.heads_qk // w.heads_v
     sw = workloads.Workload("sample", tuple(lens), heads_qk, heads_v, w.d_k, w.d_v, w.chunk,
                             w.dtype, True, True)
     x = workloads.make_inputs(sw, "cpu", seed=99)
     f = {k: workloads.to_numpy_f32(v) for k, v in x.items() if k != "cu_seqlens"}
     cu = x["cu_seqlens"].numpy().astype(np.int32)
     threads = oracle.max_threads()
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
+
+    def run():
         oracle.chunked(f["q"], f["k"], f["v"], f["g"], f["beta"], f["state"], cu_seqlens=cu,
                        chunk_size=w.chunk, threads=threads)
+
+    desc = (f"{len(lens)} sequences / {tot} tokens of the pack at {heads_v} of {w.heads_v} value "
+            f"heads (f32 chunked oracle, {threads} threads); scaled to all heads")
+    return run, tot * heads_v / w.heads_v, desc, threads
+
+
+def cpu_baseline(w: workloads.Workload, seconds: float = 15.0) -> dict:
+    run, tok, desc, threads = cpu_sample(w)
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 1 or (time.perf_counter() - t0 < seconds and reps < 100):
+        run()
         reps += 1
-        if time.perf_counter() - t0 > seconds_hint or reps >= 50:
-            break
     dt = (time.perf_counter() - t0) / reps
-    tok_s = tot * heads_v / w.heads_v / dt
-    return {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{len(lens)} sequences / {tot} tokens at {heads_v} of {w.heads_v} v heads, "
-                      f"{reps} reps; scaled to all heads"}
+    return {"value": tok / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{desc}; {reps} reps"}
 
 
 def run_reference(args, dist: Dist) -> None:
+    """The reference arm: the oracle's chunked form on the host's cores, one
+    bounded sample per step, on rank 0 only."""
     if dist.rank != 0:
         return
     w = workloads.get("ragged_prefill")
+    run, tok, desc, threads = cpu_sample(w)
+    for _ in range(args.warmup):
+        run()
     per = []
-    for i in range(args.warmup + args.steps):
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        r = cpu_sample_prefill(w, seconds_hint=0.0)
-        if i >= args.warmup:
-            per.append(time.perf_counter() - t0)
-    tok_s = r["value"]
-    r["value"] = tok_s
+        run()
+        per.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(per)
+    tok_s = tok / (ms * 1e-3)
     line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * statistics.mean(per), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
             "config": {"workload": "ragged_prefill", "tokens": w.tokens, "n_seqs": w.n_seqs,
                        "heads_qk": w.heads_qk, "heads_v": w.heads_v, "d": w.d_k,
                        "chunk": w.chunk},
-            "cpu_baseline": r,
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads,
+                             "kind": "port", "sample": desc},
             "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------------------
-def run_native(args, dist: Dist) -> None:
-    torch.cuda.set_device(dist.local)
-    dev = torch.device("cuda", dist.local)
-    stream = torch.cuda.current_stream(dev)
-    pk, pk_kind = peaks()
-    lib = _lib.load()
+# -- the GPU arm --------------------------------------------------------------------
+def shard_of(w: workloads.Workload, dist: Dist) -> HeadShard:
+    return HeadShard(dist.rank, dist.world, w.heads_qk, w.heads_v)
 
-    # -- ragged prefill (the headline) --------------------------------------
-    w = workloads.get("ragged_prefill")
+
+def bench_prefill(name: str, args, dist, dev, stream, pk, pk_kind, e2e=False, verify=False):
+    w = workloads.get(name)
+    sh = shard_of(w, dist)
     full = workloads.make_inputs(w, dev, seed=1234)
-    x = shard(full, w, dist.rank, dist.world)
-    del full
-    hq, hv = x["q"].shape[1], x["v"].shape[1]
+    x = sh.take(full)
+    hq, hv = sh.qk.stop - sh.qk.start, sh.v.stop - sh.v.start
     rule = GatedDeltaRule(chunk_size=w.chunk)
-    out = torch.empty(w.tokens, hv, w.d_v, dtype=w.dtype, device=dev)
+    lead = x["v"].shape[:-2]
+    out = torch.empty(lead + (hv, w.d_v), dtype=w.dtype, device=dev)
     st_out = torch.empty(w.n_seqs, hv, w.d_k, w.d_v, dtype=torch.float32, device=dev)
 
-    def prefill_step():
-        rule.chunked(x["q"], x["k"], x["v"], x["g"], x["beta"], x["state"],
-                     cu_seqlens=x["cu_seqlens"], out=out, state_out=st_out)
+    def step():
+        rule.chunked(x["q"], x["k"], x["v"], x["g"], x["beta"], x.get("state"),
+                     cu_seqlens=x.get("cu_seqlens"), out=out, state_out=st_out)
 
     with Clocks(dist.local) as clk:
-        total_ms, per = timed(prefill_step, args.steps, args.warmup, dist, stream)
-    assert lib.gdr_device_error() == _lib.GDR_OK
+        total_ms, per = timed(step, args.steps, args.warmup, dist, stream)
     ms = total_ms / args.steps
-    tok_s = w.tokens / (ms * 1e-3)
-    kern_ms = statistics.mean(per)  # one launch per step: the kernel's duration
-    flops = prefill_flops_per_token_head(w.chunk, w.d_k) * w.tokens * hv
-    nbytes = prefill_bytes(w, hq, hv)
-    t_flop = flops / (pk["bf16_tflops_sustained"] * 1e12)
-    t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
-    if t_flop >= t_hbm:
-        ach, peak, unit = flops / (kern_ms * 1e-3) / 1e12, pk["bf16_tflops_sustained"], "TFLOP/s"
-        bound = "tensor"
-    else:
-        ach, peak, unit = nbytes / (kern_ms * 1e-3) / 1e9, pk["hbm_gbs"], "GB/s"
-        bound = "hbm"
-    roofline = {"bound": bound, "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
-                "traffic": None, "peak_source": pk_kind,
-                "attainable_frac": max(t_flop, t_hbm) / (kern_ms * 1e-3),
-                "flops_per_launch": flops, "bytes_per_launch": nbytes,
-                "tflops": flops / (kern_ms * 1e-3) / 1e12,
-                "gbs": nbytes / (kern_ms * 1e-3) / 1e9}
+    res = {"tokens": w.tokens, "ms_per_step": ms, "value": w.tokens / (ms * 1e-3),
+           "unit": "tokens/s", "clocks": clk.summary(), "gpu_launches": args.steps,
+           "roofline": roofline(prefill_flops(w, hv), prefill_bytes(w, hq, hv),
+                                statistics.mean(per), pk, pk_kind,
+                                measured_traffic(w.tokens * hv))}
+    if verify and dist.world > 1:
+        from bunsen_b200.sharding import gather_heads
 
-    # -- end to end: host buffers through the public API ---------------------
+        step()
+        o_all = gather_heads(out, sh, head_dim=out.dim() - 2)
+        s_all = gather_heads(st_out, sh, head_dim=1)
+        if dist.rank == 0:
+            o1, s1 = rule.chunked(full["q"], full["k"], full["v"], full["g"], full["beta"],
+                                  full.get("state"), cu_seqlens=full.get("cu_seqlens"))
+            res["verified"] = bool(torch.equal(o_all, o1) and torch.equal(s_all, s1))
+    del full
+    if e2e:
+        res["e2e"] = bench_e2e(w, x, rule, out, st_out, args, dist, dev, stream)
+    return res
+
+
+def bench_e2e(w, x, rule, out, st_out, args, dist, dev, stream) -> dict:
+    """The same call through the public API with host buffers: each step
+    copies its inputs from pinned host memory, runs, and reads the output and
+    the final states back."""
     host = {k: v.to("cpu").pin_memory() for k, v in x.items()}
     dbuf = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
@@ -303,76 +336,127 @@ def run_native(args, dist: Dist) -> None:
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out_h.numel() * out_h.element_size() + st_h.numel() * st_h.element_size()
 
-    def e2e_step():
+    def step():
         for k, v in host.items():
             dbuf[k].copy_(v, non_blocking=True)
-        rule.chunked(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["g"], dbuf["beta"], dbuf["state"],
-                     cu_seqlens=dbuf["cu_seqlens"], out=out, state_out=st_out)
+        rule.chunked(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["g"], dbuf["beta"], dbuf.get("state"),
+                     cu_seqlens=dbuf.get("cu_seqlens"), out=out, state_out=st_out)
         out_h.copy_(out, non_blocking=True)
         st_h.copy_(st_out, non_blocking=True)
 
-    e2e_steps = max(1, min(args.steps, 5))
-    e2e_ms, _ = timed(e2e_step, e2e_steps, 1, dist, stream)
-    e2e = {"value": w.tokens / (e2e_ms / e2e_steps * 1e-3), "unit": "tokens/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
-    del host, dbuf, x
+    k = max(1, min(args.steps, 5))
+    total, _ = timed(step, k, 1, dist, stream)
+    return {"value": w.tokens / (total / k * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
-    # -- decode: 64 consecutive steps, states in place -----------------------
-    wd = workloads.get("decode")
+
+def bench_decode(args, dist, dev, stream, pk, pk_kind) -> dict:
+    w = workloads.get("decode")
+    sh = shard_of(w, dist)
+    x = sh.take(workloads.make_inputs(w, dev, seed=77))
+    hq, hv = sh.qk.stop - sh.qk.start, sh.v.stop - sh.v.start
     steps_per = 64
-    dx = shard(workloads.make_inputs(wd, dev, seed=77), wd, dist.rank, dist.world)
-    hvd = dx["v"].shape[2]
     gen = torch.Generator(device=dev).manual_seed(5)
-    seq = {k: torch.stack([dx[k]] + [
-        (dx[k] + 0.01 * torch.randn(dx[k].shape, generator=gen, device=dev).to(dx[k].dtype))
-        for _ in range(steps_per - 1)]) for k in ("q", "k", "v", "g", "beta")}
+
+    def jitter(t):
+        return (t + 0.01 * torch.randn(t.shape, generator=gen, device=dev).to(t.dtype))
+
+    seq = {k: torch.stack([x[k]] + [jitter(x[k]) for _ in range(steps_per - 1)])
+           for k in ("q", "k", "v", "g", "beta")}
     seq["g"] = seq["g"].clamp(max=0.0)
     seq["beta"] = seq["beta"].clamp(0.0, 1.0)
-    states = dx["state"]
-    dout = torch.empty(wd.n_seqs, 1, hvd, wd.d_v, dtype=wd.dtype, device=dev)
-    drule = GatedDeltaRule()
+    states = x["state"]
+    out = torch.empty(w.n_seqs, 1, hv, w.d_v, dtype=w.dtype, device=dev)
+    rule = GatedDeltaRule()
 
-    def decode_step():
+    def step():  # 64 consecutive decode steps, states in place
         for i in range(steps_per):
-            drule.recurrent(seq["q"][i], seq["k"][i], seq["v"][i], seq["g"][i], seq["beta"][i],
-                            states, out=dout, state_out=states)
+            rule.recurrent(seq["q"][i], seq["k"][i], seq["v"][i], seq["g"][i], seq["beta"][i],
+                           states, out=out, state_out=states)
 
-    dsteps = max(1, min(args.steps, 10))
-    d_total, d_per = timed(decode_step, dsteps, max(3, min(args.warmup, 3)), dist, stream)
-    d_ms = d_total / dsteps / steps_per
-    state_bytes = 2.0 * wd.n_seqs * hvd * wd.d_k * wd.d_v * 4 * dist.world
-    io_bytes = wd.n_seqs * dist.world * (hq * wd.d_k * 2 * 2 + hvd * wd.d_v * 2 * 2 + hvd * 8)
-    d_gbs = state_bytes / (d_ms * 1e-3) / 1e9
-    d_kern_ms = statistics.mean(d_per) / steps_per
-    per_gpu_bytes = (state_bytes + io_bytes) / dist.world
-    decode = {"metric": "decode state-update GB/s", "value": d_gbs, "unit": "GB/s",
-              "ms_per_step": d_ms, "steps_timed": dsteps * steps_per,
-              "gpu_launches": dsteps * steps_per,
-              "config": {"workload": "decode", "rows": wd.n_seqs, "heads_qk": wd.heads_qk,
-                         "heads_v": wd.heads_v, "d": wd.d_k, "state_bytes_rw": state_bytes},
-              "roofline": {"bound": "hbm", "achieved": per_gpu_bytes / (d_kern_ms * 1e-3) / 1e9,
-                           "peak": pk["hbm_gbs"], "unit": "GB/s",
-                           "frac": per_gpu_bytes / (d_kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
-                           "traffic": None, "peak_source": pk_kind}}
-    del seq, states, dx
+    k = max(1, min(args.steps, 10))
+    total, per = timed(step, k, max(3, args.warmup), dist, stream)
+    ms = total / k / steps_per
+    state_rw = 2.0 * w.n_seqs * w.heads_v * w.d_k * w.d_v * 4  # all ranks
+    io = w.n_seqs * (w.heads_qk * w.d_k * 2 * 2 + w.heads_v * w.d_v * 2 * 2 + w.heads_v * 8)
+    kern_ms = statistics.mean(per) / steps_per
+    local_bytes = (state_rw + io) / dist.world
+    return {"metric": "decode state-update GB/s", "value": state_rw / (ms * 1e-3) / 1e9,
+            "unit": "GB/s", "ms_per_step": ms, "steps_timed": k * steps_per,
+            "gpu_launches": k * steps_per,
+            "config": {"workload": "decode", "rows": w.n_seqs, "heads_qk": w.heads_qk,
+                       "heads_v": w.heads_v, "d": w.d_k, "state_bytes_rw": state_rw},
+            "roofline": {"bound": "hbm", "achieved": local_bytes / (kern_ms * 1e-3) / 1e9,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": local_bytes / (kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                         "traffic": None, "peak_source": pk_kind}}
 
+
+def bench_mixed(args, dist, dev, stream, pk, pk_kind) -> dict:
+    w = workloads.get("mixed")
+    sh = shard_of(w, dist)
+    x = sh.take(workloads.make_inputs(w, dev, seed=55))
+    hq, hv = sh.qk.stop - sh.qk.start, sh.v.stop - sh.v.start
+    pool = x["state"]  # slot s = sequence s; updated in place every step
+    rule = GatedDeltaRule()
+    out = torch.empty_like(x["v"])
+    ws = torch.empty(max(4, 4 * (w.n_seqs + 2)), dtype=torch.uint8, device=dev)
+
+    def step():
+        rule.mixed(x["q"], x["k"], x["v"], x["g"], x["beta"], pool, cu_seqlens=x["cu_seqlens"],
+                   out=out, workspace=ws)
+
+    total, per = timed(step, args.steps, args.warmup, dist, stream)
+    ms = total / args.steps
+    pre = [L for L in w.seqlens if L > 1]
+    n_dec = sum(1 for L in w.seqlens if L == 1)
+    pw = workloads.Workload("pre", tuple(pre), w.heads_qk, w.heads_v, w.d_k, w.d_v, w.chunk,
+                            w.dtype, True, True)
+    dec_bytes = n_dec * (2.0 * hv * w.d_k * w.d_v * 4
+                         + hq * w.d_k * 4 + hv * w.d_v * 4 + hv * 8)
+    nbytes = prefill_bytes(pw, hq, hv) + dec_bytes
+    flops = prefill_flops(pw, hv)
+    return {"metric": "mixed continuous batch, ms per launch", "value": ms, "unit": "ms",
+            "higher_is_better": False, "tokens": w.tokens, "prefill_tokens": sum(pre),
+            "decode_rows": n_dec, "gpu_launches": 2 * args.steps,
+            "roofline": roofline(flops, nbytes, statistics.mean(per), pk, pk_kind, None)}
+
+
+def run_native(args, dist: Dist) -> None:
+    torch.cuda.set_device(dist.local)
+    dev = torch.device("cuda", dist.local)
+    stream = torch.cuda.current_stream(dev)
+    pk, pk_kind = peaks()
+    lib = _lib.load()
+
+    rag = bench_prefill("ragged_prefill", args, dist, dev, stream, pk, pk_kind, e2e=True,
+                        verify=args.verify)
+    dense = bench_prefill("dense_prefill", args, dist, dev, stream, pk, pk_kind)
+    decode = bench_decode(args, dist, dev, stream, pk, pk_kind)
+    mixed = bench_mixed(args, dist, dev, stream, pk, pk_kind)
+    if lib.gdr_device_error() != _lib.GDR_OK:
+        raise RuntimeError("a kernel recorded a device-side failure")
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_sample_prefill(w)
-
+        cpu = cpu_baseline(workloads.get("ragged_prefill"))
     if dist.rank == 0:
-        line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": dist.world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic",
+        w = workloads.get("ragged_prefill")
+        line = {"metric": METRIC, "value": rag["value"], "unit": "tokens/s",
+                "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": rag["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": "ragged_prefill", "tokens": w.tokens, "n_seqs": w.n_seqs,
                            "max_len": max(w.seqlens), "heads_qk": w.heads_qk,
                            "heads_v": w.heads_v, "d": w.d_k, "chunk": w.chunk,
                            "parallelism": f"heads{dist.world}",
                            "l2": "inputs larger than L2 (no flush)"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": args.steps,
-                "clocks": clk.summary(), "decode": decode}
+                "roofline": rag["roofline"], "cpu_baseline": cpu, "e2e": rag["e2e"],
+                "gpu_launches": rag["gpu_launches"], "clocks": rag["clocks"],
+                "dense": {k: dense[k] for k in ("value", "unit", "ms_per_step", "roofline",
+                                                "clocks")},
+                "decode": decode, "mixed": mixed}
+        if "verified" in rag:
+            line["verified"] = rag["verified"]
         print(json.dumps(line), flush=True)
 
 
@@ -383,12 +467,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--verify", action="store_true",
+                    help="N > 1: check the gathered sharded outputs against one GPU")
     args = ap.parse_args()
     dist = Dist()
     if args.impl == "reference":
         run_reference(args, dist)
         return
-    dist.init("nccl")
+    dist.init()
     try:
         run_native(args, dist)
     finally:
