@@ -400,7 +400,11 @@ def bench_mixed(args, dist, dev, stream, pk, pk_kind) -> dict:
     pool = x["state"]  # slot s = sequence s; updated in place every step
     rule = GatedDeltaRule()
     out = torch.empty_like(x["v"])
-    ws = torch.empty(max(4, 4 * (w.n_seqs + 2)), dtype=torch.uint8, device=dev)
+    import ctypes
+
+    need = _lib.load().gdr_mixed_workspace_size(ctypes.byref(rule.params(x["q"], x["v"],
+                                                                         x["cu_seqlens"])))
+    ws = torch.empty(max(4, need), dtype=torch.uint8, device=dev)
 
     def step():
         rule.mixed(x["q"], x["k"], x["v"], x["g"], x["beta"], pool, cu_seqlens=x["cu_seqlens"],

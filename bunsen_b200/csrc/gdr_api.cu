@@ -145,6 +145,7 @@ gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, con
         workspace_bytes < gdr::mixed_workspace_bytes(p.n_seqs))
         return GDR_ERR_INVALID;
     if (!gdr::chunked_tc_supports(*params)) return GDR_ERR_UNSUPPORTED;
+    if (static_cast<int64_t>(p.n_seqs) * p.heads_v >= (int64_t{1} << 30)) return GDR_ERR_UNSUPPORTED;
     if (p.n_seqs == 0 || total_tokens(p) == 0) return GDR_OK;
     return from_cuda(gdr::launch_mixed_tc(p, q, k, v, g, beta, state_pool, state_slots, n_slots,
                                           out, static_cast<int32_t*>(workspace),
@@ -164,6 +165,7 @@ gdr_status gdr_mixed_noalloc(const gdr_params* params, const void* q, const void
     if (p.n_seqs > 0 && n_slots <= 0) return GDR_ERR_INVALID;
     if (p.n_seqs > gdr::mixed_noalloc_max_seqs()) return GDR_ERR_CAPACITY;
     if (!gdr::chunked_tc_supports(*params)) return GDR_ERR_UNSUPPORTED;
+    if (static_cast<int64_t>(p.n_seqs) * p.heads_v >= (int64_t{1} << 30)) return GDR_ERR_UNSUPPORTED;
     if (p.n_seqs == 0 || total_tokens(p) == 0) return GDR_OK;
     return from_cuda(gdr::launch_mixed_tc_noalloc(p, q, k, v, g, beta, state_pool, state_slots,
                                                   n_slots, out, static_cast<cudaStream_t>(stream)));

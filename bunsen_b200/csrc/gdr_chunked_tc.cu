@@ -247,14 +247,16 @@ __device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Nm, int 
 // One (sequence, value head): positions [t0, t0 + len) of value head h, from
 // state_in (null: zeros; may equal state_out) to state_out, both that head's
 // [d_k, d_v] f32 state. `smem` is the CTA's 1024-aligned dynamic shared
-// memory. Allocates and frees 256 TMEM columns.
+// memory. Allocates and frees 256 TMEM columns; `last_alloc` gives up the
+// CTA's right to allocate TMEM again, which only a CTA that runs no further
+// item may do.
 __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap* tm_q,
                                              const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                              const float* __restrict__ g,
                                              const float* __restrict__ beta,
                                              __nv_bfloat16* __restrict__ out, int64_t t0,
                                              int64_t len, int h, const float* state_in,
-                                             float* state_out, uint8_t* smem) {
+                                             float* state_out, uint8_t* smem, bool last_alloc) {
     uint8_t* KQ = smem + kOffKQ;
     uint8_t* VB = smem + kOffVB;
     uint8_t* AB = smem + kOffAB;
@@ -278,7 +280,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     }
     if (warp == 0) {
         tmem_alloc(&ms.tmem_base, kTmemCols);
-        tmem_relinquish();
+        if (last_alloc) tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
@@ -662,6 +664,10 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tbase, kTmemCols);
+    if (tid == 0) {  // the barriers may be initialised again by the next item
+        mbar_inval(&ms.bar_tma);
+        mbar_inval(&ms.bar_mma);
+    }
 }
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
@@ -712,26 +718,39 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     seq_span(p, s, t0, t1);
     const int64_t hs = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
     prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, h,
-                 state_in ? state_in + hs : nullptr, state_out + hs, smem);
+                 state_in ? state_in + hs : nullptr, state_out + hs, smem, true);
 }
 
 // The work list of a continuous batch, built in the caller's workspace:
 // work[0] = prefill sequences (length > 1), work[1] = decode rows (length 1),
-// then the sequence indices, prefill ones first by decreasing chunk count,
-// then the decode rows. One CTA of 1024 threads; sequences of length 0 are
-// left out.
+// work[2], work[3] = the two queues' cursors (zeroed here), work[4] = how
+// many of the `grid` CTAs start on the prefill queue, then (from
+// work[kWorkHeader]) the sequence indices, prefill ones first by decreasing
+// chunk count, then the decode rows. One CTA of 1024 threads; sequences of
+// length 0 are left out.
+//
+// The prefill share of the grid follows the work: a (prefill chunk, head)
+// item costs about kChunkCost and a (decode row, head) item about kRowCost
+// in CTA-time, measured on B200 with two CTAs per SM (a chunk's dependent
+// MMA and CUDA-core stages, against a 128 KiB state round trip sharing HBM).
 constexpr int kPlanBuckets = 1024;
+constexpr int kWorkHeader = 8;
+constexpr float kChunkCost = 1.1f, kRowCost = 1.0f;
 __global__ void __launch_bounds__(1024)
-plan_mixed(const Problem p, int32_t* work) {
+plan_mixed(const Problem p, int32_t* work, int grid) {
     __shared__ int hist[kPlanBuckets];
     __shared__ int n_pre, n_dec;
+    __shared__ unsigned long long chunks;
     const int n = p.n_seqs;
     auto bucket = [&](int64_t len) {  // descending chunk count
         const int64_t c = (len + kC - 1) / kC;
         return kPlanBuckets - 1 - static_cast<int>(c < kPlanBuckets - 1 ? c : kPlanBuckets - 1);
     };
     for (int i = threadIdx.x; i < kPlanBuckets; i += blockDim.x) hist[i] = 0;
-    if (threadIdx.x == 0) n_pre = n_dec = 0;
+    if (threadIdx.x == 0) {
+        n_pre = n_dec = 0;
+        chunks = 0;
+    }
     __syncthreads();
     for (int s = threadIdx.x; s < n; s += blockDim.x) {
         int64_t a, b;
@@ -739,6 +758,7 @@ plan_mixed(const Problem p, int32_t* work) {
         if (b - a > 1) {
             atomicAdd(&hist[bucket(b - a)], 1);
             atomicAdd(&n_pre, 1);
+            atomicAdd(&chunks, static_cast<unsigned long long>((b - a + kC - 1) / kC));
         } else if (b - a == 1) {
             atomicAdd(&n_dec, 1);
         }
@@ -753,6 +773,14 @@ plan_mixed(const Problem p, int32_t* work) {
         }
         work[0] = n_pre;
         work[1] = n_dec;
+        work[2] = 0;
+        work[3] = 0;
+        const float wp = kChunkCost * static_cast<float>(chunks);
+        const float wd = kRowCost * static_cast<float>(n_dec);
+        int pre_ctas = n_pre == 0 ? 0
+                       : n_dec == 0 ? grid
+                                    : static_cast<int>(ceilf(grid * wp / (wp + wd)));
+        work[4] = pre_ctas < grid ? pre_ctas : grid;
         n_dec = n_pre;  // cursor of the decode rows
     }
     __syncthreads();
@@ -760,41 +788,153 @@ plan_mixed(const Problem p, int32_t* work) {
         int64_t a, b;
         seq_span(p, s, a, b);
         if (b - a > 1)
-            work[2 + atomicAdd(&hist[bucket(b - a)], 1)] = s;
+            work[kWorkHeader + atomicAdd(&hist[bucket(b - a)], 1)] = s;
         else if (b - a == 1)
-            work[2 + atomicAdd(&n_dec, 1)] = s;
+            work[kWorkHeader + atomicAdd(&n_dec, 1)] = s;
     }
 }
 
-// A continuous batch: CTA row y < work[0] runs prefill sequence work[2 + y]
-// through prefill_item; the next work[1] rows run one decode row each through
-// the CUDA-core recurrent body. States live in place in `pool` at the
-// sequence's slot (slots null: the sequence index).
+// A continuous batch, persistent: each CTA pulls (sequence, value head) items
+// from two queues in the work list -- prefill segments through prefill_item,
+// decode rows through the CUDA-core recurrent body -- until both are empty.
+// The first work[4] CTAs start on the prefill queue (longest segments first)
+// and the rest on the decode rows, in proportion to the two queues' work, so
+// the latency-bound prefill does not hold the slots the bandwidth-bound decode
+// rows need; a CTA whose queue runs dry moves to the other.
+//
+// Decode rows are pipelined: while one row's state is updated in registers
+// and written back, the next row's 64 KiB state is already on its way into
+// shared memory by a bulk copy.
+constexpr uint32_t kOffDecStage = 16384;                      // 64 KiB staging
+constexpr uint32_t kOffDecBar = kOffDecStage + kD * kD * 4;   // its mbarrier
+
+struct MixedItem {
+    int qn, s, h;  // queue (0 prefill, 1 decode), sequence, value head
+    float* st;     // the head's state in the pool
+};
+
 __global__ void __launch_bounds__(kThreads, 2)
 mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
          const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
          const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
          const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
          const float* __restrict__ beta, float* pool, const int32_t* slots, int32_t n_slots,
-         __nv_bfloat16* __restrict__ out, const int32_t* work) {
+         __nv_bfloat16* __restrict__ out, int32_t* work) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = aligned_smem(smem_raw);
-    const int h = blockIdx.x, y = blockIdx.y;
-    const int n_pre = work[0], n_dec = work[1];
-    if (y >= n_pre + n_dec) return;
-    const int s = work[2 + y];
-    const int slot = slots ? slots[s] : s;
-    if (slot < 0 || slot >= n_slots) {
-        if (threadIdx.x == 0) atomicOr(&g_tc_error, 2);
-        return;
+    __shared__ MixedItem shared_item;
+    const int H = p.heads_v;
+    const int n_pre_items = work[0] * H, n_dec_items = work[1] * H;
+    const int first = static_cast<int>(blockIdx.x) < work[4] ? 0 : 1;  // 0: prefill, 1: decode
+
+    // The next item of queue qn whose slot is in the pool (bad slots are
+    // reported and skipped); every thread gets it. s < 0: the queue is empty.
+    // Thread 0 claims decode rows kDecBatch at a time with one atomic and
+    // resolves the batch's sequences and slots with independent loads, so a
+    // row costs no chain of dependent global round trips.
+    constexpr int kDecBatch = 8;
+    __shared__ MixedItem dec_cache[kDecBatch];
+    __shared__ int dec_n, dec_pos;
+    const int n_pre = work[0];
+    if (threadIdx.x == 0) dec_n = dec_pos = 0;
+    auto resolve = [&](int qn, int i, int s, MixedItem& it) {
+        const int slot = slots ? slots[s] : s;
+        it = MixedItem{qn, s, i % H, nullptr};
+        if (slot < 0 || slot >= n_slots) {
+            atomicOr(&g_tc_error, 2);
+            it.s = -2;  // skipped
+        } else {
+            it.st = pool + (static_cast<int64_t>(slot) * H + it.h) * kD * kD;
+        }
+    };
+    auto fetch = [&](int qn) -> MixedItem {
+        if (threadIdx.x == 0) {
+            MixedItem it{qn, -1, 0, nullptr};
+            if (qn == 0) {
+                for (;;) {
+                    const int i = atomicAdd(&work[2], 1);
+                    if (i >= n_pre_items) break;
+                    resolve(0, i, work[kWorkHeader + i / H], it);
+                    if (it.s >= 0) break;
+                    it.s = -1;
+                }
+            } else {
+                for (;;) {
+                    if (dec_pos == dec_n) {
+                        const int i0 = atomicAdd(&work[3], kDecBatch);
+                        const int n = n_dec_items - i0 < kDecBatch ? n_dec_items - i0 : kDecBatch;
+                        dec_n = n > 0 ? n : 0;
+                        dec_pos = 0;
+                        if (dec_n == 0) break;
+                        int seq[kDecBatch];
+#pragma unroll
+                        for (int u = 0; u < kDecBatch; ++u)
+                            seq[u] = u < dec_n ? work[kWorkHeader + n_pre + (i0 + u) / H] : 0;
+#pragma unroll
+                        for (int u = 0; u < kDecBatch; ++u)
+                            if (u < dec_n) resolve(1, i0 + u, seq[u], dec_cache[u]);
+                    }
+                    it = dec_cache[dec_pos++];
+                    if (it.s >= 0) break;
+                    it.s = -1;
+                }
+            }
+            shared_item = it;
+        }
+        __syncthreads();
+        const MixedItem it = shared_item;
+        __syncthreads();
+        return it;
+    };
+
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+        const int qn = pass == 0 ? first : 1 - first;
+        if (qn == 0) {
+#pragma unroll 1
+            for (MixedItem it = fetch(0); it.s >= 0; it = fetch(0)) {
+                int64_t t0, t1;
+                seq_span(p, it.s, t0, t1);
+                prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, it.h, it.st,
+                             it.st, smem, false);
+                __syncthreads();
+            }
+            continue;
+        }
+        float* stage = reinterpret_cast<float*>(smem + kOffDecStage);
+        uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffDecBar);
+        fence_proxy_async();  // earlier generic use of this memory, before bulk writes
+        if (threadIdx.x == 0) {
+            mbar_init(bar, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+        auto stage_state = [&](const MixedItem& it) {  // thread 0
+            mbar_expect_tx(bar, kD * kD * 4);
+            bulk_load(stage, it.st, kD * kD * 4, bar);
+        };
+        uint32_t ph = 0;
+        MixedItem cur = fetch(1);
+        if (threadIdx.x == 0 && cur.s >= 0) stage_state(cur);
+#pragma unroll 1
+        while (cur.s >= 0) {
+            if (!mbar_wait(bar, ph, kWaitLimitNs)) atomicOr(&g_tc_error, 1);
+            ph ^= 1u;
+            DecodeState st;
+            decode_load_state(stage, st);
+            fence_proxy_async();  // these reads, before the next bulk write
+            const MixedItem next = fetch(1);  // (its barriers order the reads)
+            if (threadIdx.x == 0 && next.s >= 0) stage_state(next);
+            int64_t t0, t1;
+            seq_span(p, cur.s, t0, t1);
+            decode_positions<__nv_bfloat16>(p, q, k, v, g, beta, t0, t1, cur.h, st, out, smem);
+            decode_store_state(cur.st, st);
+            cur = next;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) mbar_inval(bar);
+        __syncthreads();
     }
-    float* st = pool + (static_cast<int64_t>(slot) * p.heads_v + h) * kD * kD;
-    int64_t t0, t1;
-    seq_span(p, s, t0, t1);
-    if (y < n_pre)
-        prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, h, st, st, smem);
-    else
-        recurrent_d128_item<__nv_bfloat16>(p, q, k, v, g, beta, t0, t1, h, st, out, st, smem);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -872,7 +1012,15 @@ cudaError_t launch_chunked_tc(const Problem& p, const void* q, const void* k, co
 }
 
 size_t mixed_workspace_bytes(int n_seqs) {
-    return (static_cast<size_t>(n_seqs) + 2) * sizeof(int32_t);
+    return (static_cast<size_t>(n_seqs) + kWorkHeader) * sizeof(int32_t);
+}
+
+static int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return 148;
+    return n;
 }
 
 cudaError_t launch_mixed_tc(const Problem& p, const void* q, const void* k, const void* v,
@@ -882,8 +1030,10 @@ cudaError_t launch_mixed_tc(const Problem& p, const void* q, const void* k, cons
     cudaError_t e = make_maps(p, q, k, v, out, &mq, &mk, &mv);
     if (e != cudaSuccess) return e;
     if ((e = allow_smem(mixed_tc)) != cudaSuccess) return e;
-    plan_mixed<<<1, 1024, 0, stream>>>(p, work);
-    mixed_tc<<<dim3(p.heads_v, p.n_seqs), kThreads, kSmemBytes, stream>>>(
+    const int64_t items = static_cast<int64_t>(p.n_seqs) * p.heads_v;
+    const int grid = static_cast<int>(items < 2 * sm_count() ? items : 2 * sm_count());
+    plan_mixed<<<1, 1024, 0, stream>>>(p, work, grid);
+    mixed_tc<<<grid, kThreads, kSmemBytes, stream>>>(
         p, mq, mk, mv, static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
         static_cast<const __nv_bfloat16*>(v), g, beta, pool, slots, n_slots,
         static_cast<__nv_bfloat16*>(out), work);
@@ -892,15 +1042,16 @@ cudaError_t launch_mixed_tc(const Problem& p, const void* q, const void* k, cons
 
 // ---- gdr_mixed without a caller workspace ----------------------------------
 // The work list of gdr_mixed_noalloc lives in this fixed device array instead
-// of caller-provided memory: 2 counters plus one entry per sequence, for at
+// of caller-provided memory: an 8-word header plus one entry per sequence, for at
 // most kMixedNoAllocMaxSeqs sequences (64 KiB). Every GPU that loads the
 // library holds one copy until the process exits. All calls on a device share
 // it and it keeps the previous call's contents; the planning kernel rewrites
-// every entry a call reads, so nothing needs clearing, but calls whose work
+// every entry a call reads and zeroes the two queue cursors the launch counts
+// up from, so nothing stale is read, but calls whose work
 // overlaps on the GPU (different streams, no ordering between them) race on
 // it.
 constexpr int kMixedNoAllocMaxSeqs = GDR_MIXED_NOALLOC_MAX_SEQS;
-static __device__ __align__(256) int32_t g_mixed_scratch[2 + kMixedNoAllocMaxSeqs];
+static __device__ __align__(256) int32_t g_mixed_scratch[kWorkHeader + kMixedNoAllocMaxSeqs];
 
 // The device address of g_mixed_scratch on the current device, looked up once
 // per device (host code cannot use the symbol itself as a device pointer).

@@ -28,17 +28,37 @@ struct DecodeSmem {
     float scal[4];                     // |q|^2, |k|^2, -, q.k
 };
 
-// Positions [t0, t1) of value head h; state_in may be null (zeros) and may
-// equal state_out. `smem` holds a DecodeSmem.
+using DecodeState = float[kDecRowsPerWarp][4];
+
+// This thread's part of a [128, 128] f32 state (global or shared memory,
+// row-major): rows warp + 8 r, columns 4 lane .. 4 lane + 3.
+__device__ __forceinline__ void decode_load_state(const float* src, DecodeState& st) {
+    const int warp = threadIdx.x >> 5, col = 4 * (threadIdx.x & 31);
+#pragma unroll
+    for (int r = 0; r < kDecRowsPerWarp; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(src + (warp + kDecWarps * r) * kDecD + col);
+        st[r][0] = x.x; st[r][1] = x.y; st[r][2] = x.z; st[r][3] = x.w;
+    }
+}
+
+__device__ __forceinline__ void decode_store_state(float* dst, const DecodeState& st) {
+    const int warp = threadIdx.x >> 5, col = 4 * (threadIdx.x & 31);
+#pragma unroll
+    for (int r = 0; r < kDecRowsPerWarp; ++r)
+        *reinterpret_cast<float4*>(dst + (warp + kDecWarps * r) * kDecD + col) =
+            make_float4(st[r][0], st[r][1], st[r][2], st[r][3]);
+}
+
+// The rule over positions [t0, t1) of value head h, the state in registers.
+// `smem` holds a DecodeSmem.
 template <typename T>
-__device__ __forceinline__ void recurrent_d128_item(const Problem& p, const T* __restrict__ q,
-                                                    const T* __restrict__ k,
-                                                    const T* __restrict__ v,
-                                                    const float* __restrict__ g,
-                                                    const float* __restrict__ beta,
-                                                    int64_t t0, int64_t t1, int h,
-                                                    const float* state_in, T* __restrict__ out,
-                                                    float* state_out, uint8_t* smem) {
+__device__ __forceinline__ void decode_positions(const Problem& p, const T* __restrict__ q,
+                                                 const T* __restrict__ k,
+                                                 const T* __restrict__ v,
+                                                 const float* __restrict__ g,
+                                                 const float* __restrict__ beta, int64_t t0,
+                                                 int64_t t1, int h, DecodeState& st,
+                                                 T* __restrict__ out, uint8_t* smem) {
     constexpr int kD = kDecD, kWarps = kDecWarps, kRowsPerWarp = kDecRowsPerWarp;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     auto& sh = *reinterpret_cast<DecodeSmem*>(smem);
@@ -47,20 +67,6 @@ __device__ __forceinline__ void recurrent_d128_item(const Problem& p, const T* _
     auto& delta_s = sh.delta_s;
     auto& scal = sh.scal;
     const int col = 4 * lane;
-    float st[kRowsPerWarp][4];
-    if (state_in != nullptr) {
-        const float* src = state_in;
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) {
-            const float4 x =
-                *reinterpret_cast<const float4*>(src + (warp + kWarps * r) * kD + col);
-            st[r][0] = x.x; st[r][1] = x.y; st[r][2] = x.z; st[r][3] = x.w;
-        }
-    } else {
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) st[r][0] = st[r][1] = st[r][2] = st[r][3] = 0.f;
-    }
-
     const int hq = h / p.group;
     for (int64_t t = t0; t < t1; ++t) {
         // q and k of this position, raw, into shared memory.
@@ -128,11 +134,28 @@ __device__ __forceinline__ void recurrent_d128_item(const Problem& p, const T* _
         __syncthreads();  // qk_raw, red and delta_s are rewritten next position
     }
 
-    float* dst = state_out;
+}
+
+// Positions [t0, t1) of value head h; state_in may be null (zeros) and may
+// equal state_out. `smem` holds a DecodeSmem.
+template <typename T>
+__device__ __forceinline__ void recurrent_d128_item(const Problem& p, const T* __restrict__ q,
+                                                    const T* __restrict__ k,
+                                                    const T* __restrict__ v,
+                                                    const float* __restrict__ g,
+                                                    const float* __restrict__ beta,
+                                                    int64_t t0, int64_t t1, int h,
+                                                    const float* state_in, T* __restrict__ out,
+                                                    float* state_out, uint8_t* smem) {
+    DecodeState st;
+    if (state_in != nullptr) {
+        decode_load_state(state_in, st);
+    } else {
 #pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r)
-        *reinterpret_cast<float4*>(dst + (warp + kWarps * r) * kD + col) =
-            make_float4(st[r][0], st[r][1], st[r][2], st[r][3]);
+        for (int r = 0; r < kDecRowsPerWarp; ++r) st[r][0] = st[r][1] = st[r][2] = st[r][3] = 0.f;
+    }
+    decode_positions<T>(p, q, k, v, g, beta, t0, t1, h, st, out, smem);
+    decode_store_state(state_out, st);
 }
 
 }  // namespace gdr

@@ -108,6 +108,23 @@ def test_mixed_bad_slot_is_reported_and_skipped():
         assert torch.equal(x["pool"][s], before[s])
 
 
+def test_mixed_in_a_persistent_grid_with_more_items_than_ctas():
+    """Many more (sequence, head) items than resident CTAs: every CTA pulls
+    several items, prefill and decode, so one CTA runs several prefill items
+    (each allocating and freeing TMEM) one after another."""
+    rng = np.random.default_rng(3)
+    lens = [int(x) for x in rng.integers(2, 80, 200)] + [1] * 300 + [130, 64]
+    x = _batch(lens, hq=2, hv=4)
+    pool0 = x["pool"].clone()
+    out = GatedDeltaRule().mixed(x["q"], x["k"], x["v"], x["g"], x["beta"], x["pool"],
+                                 cu_seqlens=x["cu_seqlens"], state_slots=x["slots"])
+    torch.cuda.synchronize()
+    assert _lib.load().gdr_device_error() == _lib.GDR_OK
+    wo, wp = _expect(x, lens, pool0)
+    assert rel_err(out.float().cpu().numpy(), wo) < TOL_BF16_OUT
+    assert rel_err(x["pool"].cpu().numpy(), wp) < TOL_BF16_STATE
+
+
 def test_mixed_rejects_a_short_workspace():
     x = _batch([5, 1])
     ws = torch.empty(4, dtype=torch.uint8, device=DEV)
