@@ -82,12 +82,14 @@ constexpr int kOsStride = 160;  // bf16 row stride of the output staging tile
 struct Misc {
     float gam[kC];  // cumulative log decay within the chunk
     float gl[kC];   // the same in log2 units
+    float glf[kC];  // gl_t - log2(fk_t): a column's decay and key norm as one exponent
     float bet[kC];  // beta (0 past the end)
     float fk[kC];   // 1 / |k_t|
     float fq[kC];   // 1 / (|q_t| sqrt(d_k))
     float wk[kC];   // beta_t e^gamma_t / |k_t|
     float rr[kC];   // e^(gamma_C - gamma_t) / |k_t|
     float cq[kC];   // e^gamma_t / (|q_t| sqrt(d_k))
+    float gstage[2][kC];  // the next chunk's g and beta, landing by cp.async
     uint64_t bar_tma, bar_mma;
     uint32_t tmem_base;
     int failed;
@@ -96,6 +98,12 @@ struct Misc {
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     const __nv_bfloat162 x = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&x);
+}
+
+__device__ __forceinline__ float lg2(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -133,11 +141,9 @@ __device__ __forceinline__ void load2x32(uint32_t taddr, float (&x)[64]) {
 }
 
 // ---- the unit lower-triangular inverse ---------------------------------------
-__device__ __forceinline__ uint32_t tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+// f32 bits fed as tf32: the tensor core reads the top 19 bits (truncation,
+// relative error below 2^-10, inside what the bf16 use of A tolerates).
+__device__ __forceinline__ uint32_t tf32(float x) { return __float_as_uint(x); }
 
 // c[nt] (16 x 8 tiles nt = 0, 1) += A (16 x 16) B (16 x 16), f32 in shared
 // memory with row strides lda, ldb, through tf32 mma.sync.
@@ -181,9 +187,37 @@ __device__ __forceinline__ void store16(float* M, int ld, const float (&c)[2][4]
 //  N  N_ij = X_ii L_ij for the six blocks below the diagonal (tf32 mma.sync);
 //  then X_ij = -sum_{k=j}^{i-1} N_ik X_kj, one block diagonal per level, each
 //  product issued as soon as its X_kj exists, so three levels of one product
-//  each follow N. `Nm` holds the six N blocks (16 x 20 f32 each).
-constexpr int kLdN = 20;
-__device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Nm, int tid) {
+//  each follow N. The six N blocks live in the strictly upper part of Lf,
+//  which nothing reads.
+constexpr int kLdN = kLd;
+
+// Row i, columns [32 hh, 32 hh + 32) of A diag(fac) as bf16 into the
+// swizzled K-major operand `dst` (zero above the diagonal).
+__device__ __forceinline__ void a_row(const float* X, const float* fac, uint8_t* dst, int i,
+                                      int hh) {
+    float a[32];
+    if (32 * hh > i) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) a[c] = 0.f;
+    } else {
+        const float4* src = reinterpret_cast<const float4*>(X + i * kLd + 32 * hh);
+        const float4* f4 = reinterpret_cast<const float4*>(fac + 32 * hh);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 x = src[c], f = f4[c];
+            a[4 * c + 0] = x.x * f.x;
+            a[4 * c + 1] = x.y * f.y;
+            a[4 * c + 2] = x.z * f.z;
+            a[4 * c + 3] = x.w * f.w;
+        }
+    }
+    store_half_row_sw128(dst, i, 4 * hh, a);
+}
+
+// Also writes the two operands A diag(fac0) (at AB) and A diag(fac1) (at AB +
+// kTileBytes): rows 0..47 while the last level runs, rows 48..63 after it.
+__device__ void unit_lower_inverse_64(float* Lf, float* X, int tid, const float* fac0,
+                                      const float* fac1, uint8_t* AB) {
     const int warp = tid >> 5, lane = tid & 31;
     if (tid < 64) {
         const int b = tid >> 4, m = tid & 15;
@@ -210,7 +244,12 @@ __device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Nm, int 
     const int pi = warp < 3 ? warp + 1 : (warp < 5 ? warp - 1 : 3);
     const int pj = warp < 3 ? warp : (warp < 5 ? warp - 3 : 0);
     auto Xb = [&](int i, int j) { return X + (16 * i) * kLd + 16 * j; };
-    auto Nb = [&](int w) { return Nm + w * 16 * kLdN; };
+    // N block w sits at (row, column) block (0,1) (2,3) (0,2) (0,3) (1,2) (1,3) of Lf.
+    auto Nb = [&](int w) {
+        const int rb = w == 1 ? 2 : (w < 4 ? 0 : 1);
+        const int cb = w == 0 ? 1 : (w == 2 || w == 4 ? 2 : 3);
+        return Lf + (16 * rb) * kLd + 16 * cb;
+    };
     if (warp < 6) {
         float c[2][4] = {};
         mma16_tf32(Xb(pi, pi), kLd, Lf + (16 * pi) * kLd + 16 * pj, kLd, c, lane);
@@ -236,12 +275,24 @@ __device__ void unit_lower_inverse_64(const float* Lf, float* X, float* Nm, int 
         mma16_tf32(Nb(4), kLdN, Xb(1, 0), kLd, c, lane);
     }
     __syncthreads();
-    // Level 3: X_30 += N_32 X_20.
+    // Level 3: X_30 += N_32 X_20; meanwhile the final rows 0..47 are written.
     if (warp == 5) {
         mma16_tf32(Nb(2), kLdN, Xb(2, 0), kLd, c, lane);
         store16(Xb(3, 0), kLd, c, -1.f, lane);
+    } else {
+        // 192 row tasks (rows 0..47 x two matrices x two halves) on warps 0-4
+        // and the first warp after warp 5.
+        const int t = tid < 160 ? tid : tid - 32;
+        if (t < 192) {
+            const int i = t % 48, mtx = (t / 48) & 1, hh = t / 96;
+            a_row(X, mtx ? fac1 : fac0, AB + mtx * kTileBytes, i, hh);
+        }
     }
     __syncthreads();
+    if (tid < 64) {
+        const int i = 48 + (tid & 15), mtx = (tid >> 4) & 1, hh = tid >> 5;
+        a_row(X, mtx ? fac1 : fac0, AB + mtx * kTileBytes, i, hh);
+    }
 }
 
 // One (sequence, value head): positions [t0, t0 + len) of value head h, from
@@ -306,51 +357,57 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         tma_load_3d(KQ + 3 * kTileBytes, tm_q, &ms.bar_tma, 64, hq, tok);
         tma_load_3d(VB + 0 * kTileBytes, tm_v, &ms.bar_tma, 0, h, tok);
         tma_load_3d(VB + 1 * kTileBytes, tm_v, &ms.bar_tma, 64, h, tok);
-        if (ci + 1 < n_chunks) {
-            const int nt = tok + kC;
-            tma_prefetch_3d(tm_k, 0, hq, nt);
-            tma_prefetch_3d(tm_k, 64, hq, nt);
-            tma_prefetch_3d(tm_q, 0, hq, nt);
-            tma_prefetch_3d(tm_q, 64, hq, nt);
-            tma_prefetch_3d(tm_v, 0, h, nt);
-            tma_prefetch_3d(tm_v, 64, h, nt);
-        }
     };
-    // Warp 0: chunk ci's gates (positions 2 lane, 2 lane + 1; zero past the
-    // end) into registers ...
-    auto load_gates = [&](int ci, float (&pg)[2], float (&pb)[2]) {
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int64_t pos = static_cast<int64_t>(ci) * kC + 2 * lane + u;
-            const bool in = pos < len;
-            const int64_t gi = (t0 + pos) * p.heads_v + h;
-            pg[u] = in ? g[gi] : 0.f;
-            pb[u] = in ? beta[gi] : 0.f;
-        }
+    auto prefetch_tiles = [&](int ci) {  // one thread: chunk ci's tiles into L2
+        const int tok = static_cast<int>(t0 + static_cast<int64_t>(ci) * kC);
+        tma_prefetch_3d(tm_k, 0, hq, tok);
+        tma_prefetch_3d(tm_k, 64, hq, tok);
+        tma_prefetch_3d(tm_q, 0, hq, tok);
+        tma_prefetch_3d(tm_q, 64, hq, tok);
+        tma_prefetch_3d(tm_v, 0, h, tok);
+        tma_prefetch_3d(tm_v, 64, h, tok);
     };
-    // ... then into shared memory, the log decay as its running sum.
-    auto put_gates = [&](const float (&pg)[2], const float (&pb)[2]) {
-        float incl = pg[0] + pg[1];
+    // Threads 0..127: chunk ci's g (tid < 64) or beta into ms.gstage by 4-byte
+    // cp.async (zero-filled past the end), so no register waits for them.
+    auto stage_gates = [&](int ci) {
+        const int t = tid & (kC - 1), which = tid >> 6;
+        const int64_t pos = static_cast<int64_t>(ci) * kC + t;
+        const int64_t at = pos < len ? pos : len - 1;
+        const float* src = (which ? beta : g) + (t0 + at) * p.heads_v + h;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(
+                         smem_u32(&ms.gstage[which][t])),
+                     "l"(src), "r"(pos < len ? 4 : 0)
+                     : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto gates_landed = [] { asm volatile("cp.async.wait_group 0;" ::: "memory"); };
+    // Warp 0: the staged gates into the chunk's arrays, the log decay as its
+    // running sum (positions 2 lane, 2 lane + 1).
+    auto put_gates = [&] {
+        const float pg0 = ms.gstage[0][2 * lane], pg1 = ms.gstage[0][2 * lane + 1];
+        float incl = pg0 + pg1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float y = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += y;
         }
-        const float g0 = incl - pg[1], g1 = incl;
+        const float g0 = incl - pg1, g1 = incl;
         ms.gam[2 * lane] = g0;
         ms.gam[2 * lane + 1] = g1;
         ms.gl[2 * lane] = g0 * kLog2e;
         ms.gl[2 * lane + 1] = g1 * kLog2e;
-        ms.bet[2 * lane] = pb[0];
-        ms.bet[2 * lane + 1] = pb[1];
+        ms.bet[2 * lane] = ms.gstage[1][2 * lane];
+        ms.bet[2 * lane + 1] = ms.gstage[1][2 * lane + 1];
     };
 
     if (tid == 0 && n_chunks > 0) issue_tiles(0);
-    float pg[2] = {0.f, 0.f}, pb[2] = {0.f, 0.f};
-    if (warp == 0 && n_chunks > 0) {
-        load_gates(0, pg, pb);
-        put_gates(pg, pb);
+    if (tid == kThreads - 32 && n_chunks > 1) prefetch_tiles(1);
+    if (tid < 2 * kC && n_chunks > 0) {
+        stage_gates(0);
+        gates_landed();
     }
+    __syncthreads();
+    if (warp == 0 && n_chunks > 0) put_gates();
 
     // The initial state, transposed into TMEM: lane d holds S[:, d].
     {
@@ -415,7 +472,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             float d = 0.f;
 #pragma unroll
             for (int j = 0; j < 32; ++j) d = (j == lane) ? gr[j] : d;
-            ms.fk[row] = l2_factor(p, d);
+            const float fk = l2_factor(p, d);
+            ms.fk[row] = fk;
+            ms.glf[row] = ms.gl[row] - lg2(fk);
         }
         tc_fence_before();
         __syncthreads();
@@ -439,21 +498,19 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
 #pragma unroll
                 for (int jj = 0; jj < 32; ++jj) v[jj] = 0.f;
             } else {
-                const float gli = ms.gl[i];
+                // rowf_i fk_j e^(gamma_i - gamma_j) = 2^(a_i - glf_j): one
+                // exponential carries the decay and both norm factors.
                 const float rowf = key_row ? ms.bet[i] * ms.fk[i] : ms.fq[i];
+                const float a = ms.gl[i] + lg2(rowf);
                 const int lim = key_row ? i : i + 1;  // j < lim survives
-                const float4* gl4 = reinterpret_cast<const float4*>(ms.gl + 32 * hf);
-                const float4* fk4 = reinterpret_cast<const float4*>(ms.fk + 32 * hf);
+                const float4* glf4 = reinterpret_cast<const float4*>(ms.glf + 32 * hf);
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    const float4 gl = gl4[c], fk = fk4[c];
-                    const float glv[4] = {gl.x, gl.y, gl.z, gl.w};
-                    const float fkv[4] = {fk.x, fk.y, fk.z, fk.w};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int jj = 4 * c + u;
-                        v[jj] = rowf * (fkv[u] * gr[jj]) * ex2(gli - glv[u]);
-                    }
+                    const float4 b = glf4[c];
+                    v[4 * c + 0] = gr[4 * c + 0] * ex2(a - b.x);
+                    v[4 * c + 1] = gr[4 * c + 1] * ex2(a - b.y);
+                    v[4 * c + 2] = gr[4 * c + 2] * ex2(a - b.z);
+                    v[4 * c + 3] = gr[4 * c + 3] * ex2(a - b.w);
                 }
                 if (rblk == hf) {
 #pragma unroll
@@ -470,30 +527,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             }
         }
         __syncthreads();
-        // (g) A = (I + L)^-1.
-        unit_lower_inverse_64(Lf, X, reinterpret_cast<float*>(AB), tid);
-        // (h) The two column scalings of A, as bf16 K-major B operands.
-        {
-            const int mtx = tid >> 7, hh = (tid >> 6) & 1, i = tid & 63;
-            const float* fac = mtx ? ms.wk : ms.bet;
-            const float4* src = reinterpret_cast<const float4*>(X + i * kLd + 32 * hh);
-            const float4* f4 = reinterpret_cast<const float4*>(fac + 32 * hh);
-            float a[32];
-            if (32 * hh > i) {  // above the diagonal: uniform per warp
-#pragma unroll
-                for (int c = 0; c < 32; ++c) a[c] = 0.f;
-            } else {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float4 x = src[c], f = f4[c];
-                    a[4 * c + 0] = x.x * f.x;
-                    a[4 * c + 1] = x.y * f.y;
-                    a[4 * c + 2] = x.z * f.z;
-                    a[4 * c + 3] = x.w * f.w;
-                }
-            }
-            store_half_row_sw128(AB + mtx * kTileBytes, i, 4 * hh, a);
-        }
+        // (g) A = (I + L)^-1. Meanwhile the chunk after next warms L2.
+        if (tid == kThreads - 32 && ci + 2 < n_chunks) prefetch_tiles(ci + 2);
+        unit_lower_inverse_64(Lf, X, tid, ms.bet, ms.wk, AB);
         fence_proxy_async();
         __syncthreads();
         // (i) G2: U^T = V^T Au^T -> R1; W^T = K^T Aw^T -> R0.
@@ -509,6 +545,8 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                           id, ks > 0);
             umma_commit(&ms.bar_mma);
         }
+        // The next chunk's gates start loading (they are published in (p)).
+        if (tid < 2 * kC && ci + 1 < n_chunks) stage_gates(ci + 1);
         // (j) While G2 runs: S^T -> bf16 operand; S^T <- e^gamma_C S^T.
         {
 #pragma unroll 1
@@ -573,6 +611,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             }
             store_half_row_sw128(ST + 16384, row, 4 * hf, vn);
         }
+        if (tid < 2 * kC) gates_landed();
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
@@ -590,10 +629,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             umma_commit(&ms.bar_mma);
         }
         // (p) The next chunk's gates (this chunk's are no longer read).
-        if (warp == 0 && ci + 1 < n_chunks) {
-            load_gates(ci + 1, pg, pb);
-            put_gates(pg, pb);
-        }
+        if (warp == 0 && ci + 1 < n_chunks) put_gates();
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
         // (r) The next chunk's tiles load while this chunk's output is written.
