@@ -70,10 +70,8 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColG = 128, kColR0 = 128, kColR1 = 192;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
-constexpr int kLd = 68;  // f32 row stride of L and A (conflict-free fragments)
 constexpr uint32_t kOffKQ = 0, kOffVB = 32768, kOffAB = 49152, kOffIN = 65536;
 constexpr uint32_t kOffST = 73728, kOffMisc = 110592;
-constexpr uint32_t kOffX = kC * kLd * 4;  // A after L inside ST
 constexpr uint32_t kTileBytes = 8192;     // one 64 x 64 bf16 TMA box
 constexpr uint32_t kSmemBytes = kOffMisc + 3072 + 1024;  // + alignment slack
 constexpr float kLog2e = 1.4426950408889634f;
@@ -141,157 +139,152 @@ __device__ __forceinline__ void load2x32(uint32_t taddr, float (&x)[64]) {
 }
 
 // ---- the unit lower-triangular inverse ---------------------------------------
-// f32 bits fed as tf32: the tensor core reads the top 19 bits (truncation,
-// relative error below 2^-10, inside what the bf16 use of A tolerates).
-__device__ __forceinline__ uint32_t tf32(float x) { return __float_as_uint(x); }
-
-// c[nt] (16 x 8 tiles nt = 0, 1) += A (16 x 16) B (16 x 16), f32 in shared
-// memory with row strides lda, ldb, through tf32 mma.sync.
-__device__ __forceinline__ void mma16_tf32(const float* A, int lda, const float* B, int ldb,
-                                           float (&c)[2][4], int lane) {
-    const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-        const uint32_t a0 = tf32(A[g * lda + 8 * ks + t]);
-        const uint32_t a1 = tf32(A[(g + 8) * lda + 8 * ks + t]);
-        const uint32_t a2 = tf32(A[g * lda + 8 * ks + t + 4]);
-        const uint32_t a3 = tf32(A[(g + 8) * lda + 8 * ks + t + 4]);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            const uint32_t b0 = tf32(B[(8 * ks + t) * ldb + 8 * nt + g]);
-            const uint32_t b1 = tf32(B[(8 * ks + t + 4) * ldb + 8 * nt + g]);
-            asm volatile(
-                "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
-                "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-                : "+f"(c[nt][0]), "+f"(c[nt][1]), "+f"(c[nt][2]), "+f"(c[nt][3])
-                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-        }
-    }
+// 64 x 64 bf16 tiles in the 128-byte-swizzled row layout of the MMA operands:
+// element (row, col) at row * 128 + ((col / 8) ^ (row % 8)) * 16 + (col % 8) * 2.
+__device__ __forceinline__ uint32_t sw_off(int row, int col) {
+    return row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + ((col & 7) << 1);
 }
 
-__device__ __forceinline__ void store16(float* M, int ld, const float (&c)[2][4], float sign,
-                                        int lane) {
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// c[nt] (two 16 x 8 tiles) += A B for the 16 x 16 blocks A at (ar, ac) of tile
+// `ta` and B at (br, bc) of tile `tb` (B stored [k][n]), bf16 operands through
+// ldmatrix, f32 accumulation (mma.sync m16n8k16).
+__device__ __forceinline__ void mma16_bf16(uint32_t ta, int ar, int ac, uint32_t tb, int br,
+                                           int bc, float (&c)[2][4], int lane) {
+    const int i = lane >> 3, j = lane & 7;
+    uint32_t a[4], b[4];
+    ldsm_x4(a, ta + sw_off(ar + j + 8 * (i & 1), ac + 8 * (i >> 1)));
+    ldsm_x4_trans(b, tb + sw_off(br + j + 8 * (i & 1), bc + 8 * (i >> 1)));
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+            "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(c[nt][0]), "+f"(c[nt][1]), "+f"(c[nt][2]), "+f"(c[nt][3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[2 * nt]), "r"(b[2 * nt + 1]));
+}
+
+// sign * c as bf16 at the 16 x 16 block (r0, c0) of a tile; with `fac`, each
+// column scaled by fac[column].
+__device__ __forceinline__ void store16_bf16(uint8_t* tile, int r0, int c0, const float (&c)[2][4],
+                                             float sign, const float* fac, int lane) {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-        M[g * ld + 8 * nt + 2 * t] = sign * c[nt][0];
-        M[g * ld + 8 * nt + 2 * t + 1] = sign * c[nt][1];
-        M[(g + 8) * ld + 8 * nt + 2 * t] = sign * c[nt][2];
-        M[(g + 8) * ld + 8 * nt + 2 * t + 1] = sign * c[nt][3];
+        const int col = c0 + 8 * nt + 2 * t;
+        const float f0 = fac ? sign * fac[col] : sign, f1 = fac ? sign * fac[col + 1] : sign;
+        *reinterpret_cast<uint32_t*>(tile + sw_off(r0 + g, col)) =
+            pack_bf16(c[nt][0] * f0, c[nt][1] * f1);
+        *reinterpret_cast<uint32_t*>(tile + sw_off(r0 + g + 8, col)) =
+            pack_bf16(c[nt][2] * f0, c[nt][3] * f1);
     }
 }
 
-// A = (I + L)^-1 for the strictly lower 64 x 64 L in `Lf` into `X` (both f32,
-// row stride kLd; X zero above the diagonal), with 16 x 16 blocks:
-//  D  the diagonal blocks X_ii = (I + L_ii)^-1 by exact forward substitution;
-//  N  N_ij = X_ii L_ij for the six blocks below the diagonal (tf32 mma.sync);
-//  then X_ij = -sum_{k=j}^{i-1} N_ik X_kj, one block diagonal per level, each
-//  product issued as soon as its X_kj exists, so three levels of one product
-//  each follow N. The six N blocks live in the strictly upper part of Lf,
-//  which nothing reads.
-constexpr int kLdN = kLd;
+// Where the solve's inputs and scratch live (inside the ST region).
+constexpr uint32_t kLdStride = 17;                        // f32 diagonal blocks
+constexpr uint32_t kOffLd = 0;                            // 4 x 16 x 17 f32
+constexpr uint32_t kOffLb = 8192;                         // L, bf16 64 x 64
+constexpr uint32_t kOffXb = kOffLb + 8192;                // A, bf16 64 x 64
+constexpr uint32_t kOffNb = kOffXb + 8192;                // the N blocks, bf16
 
-// Row i, columns [32 hh, 32 hh + 32) of A diag(fac) as bf16 into the
-// swizzled K-major operand `dst` (zero above the diagonal).
-__device__ __forceinline__ void a_row(const float* X, const float* fac, uint8_t* dst, int i,
-                                      int hh) {
-    float a[32];
-    if (32 * hh > i) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) a[c] = 0.f;
-    } else {
-        const float4* src = reinterpret_cast<const float4*>(X + i * kLd + 32 * hh);
-        const float4* f4 = reinterpret_cast<const float4*>(fac + 32 * hh);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const float4 x = src[c], f = f4[c];
-            a[4 * c + 0] = x.x * f.x;
-            a[4 * c + 1] = x.y * f.y;
-            a[4 * c + 2] = x.z * f.z;
-            a[4 * c + 3] = x.w * f.w;
-        }
-    }
-    store_half_row_sw128(dst, i, 4 * hh, a);
-}
-
-// Also writes the two operands A diag(fac0) (at AB) and A diag(fac1) (at AB +
-// kTileBytes): rows 0..47 while the last level runs, rows 48..63 after it.
-__device__ void unit_lower_inverse_64(float* Lf, float* X, int tid, const float* fac0,
-                                      const float* fac1, uint8_t* AB) {
+// A = (I + L)^-1 for the strictly lower 64 x 64 L, in 16 x 16 blocks:
+//  D  the diagonal blocks X_ii = (I + L_ii)^-1, exact f32 forward
+//     substitution from `Ld` (f32, the four diagonal blocks of L);
+//  N  N_ij = X_ii L_ij for the six blocks below the diagonal;
+//  then X_ij = -sum_{k=j}^{i-1} N_ik X_kj, one block diagonal per level,
+//  each product issued as soon as its X_kj exists, so three levels of one
+//  product each follow N. Products are bf16 mma.sync with f32 accumulation
+//  on `Lb` (L in bf16). Every block of A goes out, as it is found, as bf16 to
+//  `Xb` (for the later levels) and scaled by the column factors fac0 / fac1
+//  to the two G2 operands at AB and AB + kTileBytes, which get their zero
+//  blocks above the diagonal here too.
+__device__ void unit_lower_inverse_64(uint8_t* ST, int tid, const float* fac0, const float* fac1,
+                                      uint8_t* AB) {
     const int warp = tid >> 5, lane = tid & 31;
+    const float* Ld = reinterpret_cast<const float*>(ST + kOffLd);
+    uint8_t* Xb = ST + kOffXb;
+    uint8_t* Nb = ST + kOffNb;
+    const uint32_t sLb = smem_u32(ST + kOffLb), sXb = smem_u32(Xb), sNb = smem_u32(Nb);
+    uint8_t* Au = AB;
+    uint8_t* Aw = AB + kTileBytes;
     if (tid < 64) {
         const int b = tid >> 4, m = tid & 15;
-        const float* Lb = Lf + (16 * b) * kLd + 16 * b;
+        const float* Lb = Ld + (16 * b) * kLdStride;
         float x[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) x[r] = (r == m) ? 1.f : 0.f;
 #pragma unroll
         for (int s = 0; s < 15; ++s)
 #pragma unroll
-            for (int r = s + 1; r < 16; ++r) x[r] = fmaf(-Lb[r * kLd + s], x[s], x[r]);
+            for (int r = s + 1; r < 16; ++r) x[r] = fmaf(-Lb[r * kLdStride + s], x[s], x[r]);
+        const int col = 16 * b + m;
+        const float f0 = fac0[col], f1 = fac1[col];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) X[(16 * b + r) * kLd + 16 * b + m] = x[r];
-    } else if (tid < 128) {
-        // Blocks (0, 1) and (2, 3) above the diagonal are read as zeros (the
-        // rest of the upper triangle is never read).
-        for (int e = tid - 64; e < 2 * 256; e += 64) {
-            const int ib = (e >> 8) * 2, r = (e >> 4) & 15, c = e & 15;
-            X[(16 * ib + r) * kLd + 16 * (ib + 1) + c] = 0.f;
+        for (int r = 0; r < 16; ++r) {
+            const uint32_t off = sw_off(16 * b + r, col);
+            *reinterpret_cast<__nv_bfloat16*>(Xb + off) = __float2bfloat16_rn(x[r]);
+            *reinterpret_cast<__nv_bfloat16*>(Au + off) = __float2bfloat16_rn(x[r] * f0);
+            *reinterpret_cast<__nv_bfloat16*>(Aw + off) = __float2bfloat16_rn(x[r] * f1);
+        }
+    } else {
+        // The six blocks above the block diagonal of both G2 operands are zero:
+        // 6 blocks x 16 rows x 2 16-byte chunks x 2 operands.
+        for (int e = tid - 64; e < 6 * 16 * 2 * 2; e += kThreads - 64) {
+            const int blk = e >> 6, r = (e >> 2) & 15, half = (e >> 1) & 1, mtx = e & 1;
+            const int ib = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+            const int jb = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+            const int row = 16 * ib + r, col = 16 * jb + 8 * half;
+            *reinterpret_cast<uint4*>((mtx ? Aw : Au) + sw_off(row, col)) = make_uint4(0, 0, 0, 0);
         }
     }
     __syncthreads();
     // Block pairs (i, j) of N, by warp: (1,0) (2,1) (3,2) (2,0) (3,1) (3,0).
     const int pi = warp < 3 ? warp + 1 : (warp < 5 ? warp - 1 : 3);
     const int pj = warp < 3 ? warp : (warp < 5 ? warp - 3 : 0);
-    auto Xb = [&](int i, int j) { return X + (16 * i) * kLd + 16 * j; };
-    // N block w sits at (row, column) block (0,1) (2,3) (0,2) (0,3) (1,2) (1,3) of Lf.
-    auto Nb = [&](int w) {
-        const int rb = w == 1 ? 2 : (w < 4 ? 0 : 1);
-        const int cb = w == 0 ? 1 : (w == 2 || w == 4 ? 2 : 3);
-        return Lf + (16 * rb) * kLd + 16 * cb;
-    };
     if (warp < 6) {
         float c[2][4] = {};
-        mma16_tf32(Xb(pi, pi), kLd, Lf + (16 * pi) * kLd + 16 * pj, kLd, c, lane);
-        store16(Nb(warp), kLdN, c, 1.f, lane);
+        mma16_bf16(sXb, 16 * pi, 16 * pi, sLb, 16 * pi, 16 * pj, c, lane);
+        store16_bf16(Nb, 16 * pi, 16 * pj, c, 1.f, nullptr, lane);
     }
     __syncthreads();
-    float c[2][4] = {};
     // Level 1: X_10, X_21, X_32; and the parts of X_20, X_31, X_30 that only
     // need diagonal blocks.
+    float c[2][4] = {};
+    auto put = [&](int i, int j, bool keep) {  // X_ij = -c
+        if (keep) store16_bf16(Xb, 16 * i, 16 * j, c, -1.f, nullptr, lane);
+        store16_bf16(Au, 16 * i, 16 * j, c, -1.f, fac0, lane);
+        store16_bf16(Aw, 16 * i, 16 * j, c, -1.f, fac1, lane);
+    };
     if (warp < 6) {
-        mma16_tf32(Nb(warp), kLdN, Xb(pj, pj), kLd, c, lane);  // N_ij X_jj
-        if (warp < 3) store16(Xb(pi, pj), kLd, c, -1.f, lane);
+        mma16_bf16(sNb, 16 * pi, 16 * pj, sXb, 16 * pj, 16 * pj, c, lane);  // N_ij X_jj
+        if (warp < 3) put(pi, pj, warp < 2);  // X_10, X_21 feed level 2
     }
     __syncthreads();
     // Level 2: X_20 += N_21 X_10, X_31 += N_32 X_21; X_30 gathers N_31 X_10.
     if (warp == 3) {
-        mma16_tf32(Nb(1), kLdN, Xb(1, 0), kLd, c, lane);
-        store16(Xb(2, 0), kLd, c, -1.f, lane);
+        mma16_bf16(sNb, 32, 16, sXb, 16, 0, c, lane);
+        put(2, 0, true);
     } else if (warp == 4) {
-        mma16_tf32(Nb(2), kLdN, Xb(2, 1), kLd, c, lane);
-        store16(Xb(3, 1), kLd, c, -1.f, lane);
+        mma16_bf16(sNb, 48, 32, sXb, 32, 16, c, lane);
+        put(3, 1, false);
     } else if (warp == 5) {
-        mma16_tf32(Nb(4), kLdN, Xb(1, 0), kLd, c, lane);
+        mma16_bf16(sNb, 48, 16, sXb, 16, 0, c, lane);
     }
     __syncthreads();
-    // Level 3: X_30 += N_32 X_20; meanwhile the final rows 0..47 are written.
+    // Level 3: X_30 += N_32 X_20.
     if (warp == 5) {
-        mma16_tf32(Nb(2), kLdN, Xb(2, 0), kLd, c, lane);
-        store16(Xb(3, 0), kLd, c, -1.f, lane);
-    } else {
-        // 192 row tasks (rows 0..47 x two matrices x two halves) on warps 0-4
-        // and the first warp after warp 5.
-        const int t = tid < 160 ? tid : tid - 32;
-        if (t < 192) {
-            const int i = t % 48, mtx = (t / 48) & 1, hh = t / 96;
-            a_row(X, mtx ? fac1 : fac0, AB + mtx * kTileBytes, i, hh);
-        }
-    }
-    __syncthreads();
-    if (tid < 64) {
-        const int i = 48 + (tid & 15), mtx = (tid >> 4) & 1, hh = tid >> 5;
-        a_row(X, mtx ? fac1 : fac0, AB + mtx * kTileBytes, i, hh);
+        mma16_bf16(sNb, 48, 32, sXb, 32, 0, c, lane);
+        put(3, 0, false);
     }
 }
 
@@ -314,8 +307,6 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     uint8_t* IN = smem + kOffIN;
     uint8_t* ST = smem + kOffST;
     Misc& ms = *reinterpret_cast<Misc*>(smem + kOffMisc);
-    float* Lf = reinterpret_cast<float*>(ST);
-    float* X = reinterpret_cast<float*>(ST + kOffX);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int qd = warp & 3, hf = warp >> 2;
@@ -518,10 +509,15 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 }
             }
             if (key_row) {
-                float4* dst = reinterpret_cast<float4*>(Lf + i * kLd + 32 * hf);
+                // L in bf16 for the solve's products; its diagonal 16 x 16
+                // block in f32 for the exact forward substitution.
+                store_half_row_sw128(ST + kOffLb, i, 4 * hf, v);
+                if (rblk == hf) {
+                    float* ld = reinterpret_cast<float*>(ST + kOffLd) + i * kLdStride;
+                    const bool upper = (i >> 4) & 1;
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                    for (int s2 = 0; s2 < 16; ++s2) ld[s2] = upper ? v[16 + s2] : v[s2];
+                }
             } else {
                 store_half_row_sw128(IN, i, 4 * hf, v);
             }
@@ -529,7 +525,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         __syncthreads();
         // (g) A = (I + L)^-1. Meanwhile the chunk after next warms L2.
         if (tid == kThreads - 32 && ci + 2 < n_chunks) prefetch_tiles(ci + 2);
-        unit_lower_inverse_64(Lf, X, tid, ms.bet, ms.wk, AB);
+        unit_lower_inverse_64(ST, tid, ms.bet, ms.wk, AB);
         fence_proxy_async();
         __syncthreads();
         // (i) G2: U^T = V^T Au^T -> R1; W^T = K^T Aw^T -> R0.
