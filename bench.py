@@ -369,10 +369,18 @@ def bench_decode(args, dist, dev, stream, pk, pk_kind) -> dict:
     out = torch.empty(w.n_seqs, 1, hv, w.d_v, dtype=w.dtype, device=dev)
     rule = GatedDeltaRule()
 
-    def step():  # 64 consecutive decode steps, states in place
+    def steps():  # 64 consecutive decode steps, states in place
         for i in range(steps_per):
             rule.recurrent(seq["q"][i], seq["k"][i], seq["v"][i], seq["g"][i], seq["beta"][i],
                            states, out=out, state_out=states)
+
+    # The 64 steps are captured once in a CUDA graph and replayed per step.
+    steps()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        steps()
+    step = graph.replay
 
     k = max(1, min(args.steps, 10))
     total, per = timed(step, k, max(3, args.warmup), dist, stream)
@@ -381,8 +389,9 @@ def bench_decode(args, dist, dev, stream, pk, pk_kind) -> dict:
     io = w.n_seqs * (w.heads_qk * w.d_k * 2 * 2 + w.heads_v * w.d_v * 2 * 2 + w.heads_v * 8)
     kern_ms = statistics.mean(per) / steps_per
     local_bytes = (state_rw + io) / dist.world
+    del graph
     return {"metric": "decode state-update GB/s", "value": state_rw / (ms * 1e-3) / 1e9,
-            "unit": "GB/s", "ms_per_step": ms, "steps_timed": k * steps_per,
+            "unit": "GB/s", "ms_per_step": ms, "steps_timed": k * steps_per, "cuda_graph": True,
             "gpu_launches": k * steps_per,
             "config": {"workload": "decode", "rows": w.n_seqs, "heads_qk": w.heads_qk,
                        "heads_v": w.heads_v, "d": w.d_k, "state_bytes_rw": state_rw},

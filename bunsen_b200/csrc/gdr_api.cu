@@ -18,6 +18,7 @@ cudaError_t launch_chunked_tc(const Problem&, const void*, const void*, const vo
                               const float*, const float*, const float*, void*, float*,
                               cudaStream_t);
 cudaError_t take_device_error(int* flag);
+cudaError_t launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream);
 int mixed_noalloc_max_seqs();
 cudaError_t launch_mixed_tc_noalloc(const Problem&, const void*, const void*, const void*,
                                     const float*, const float*, float*, const int32_t*, int32_t,
@@ -169,6 +170,12 @@ gdr_status gdr_mixed_noalloc(const gdr_params* params, const void* q, const void
     if (p.n_seqs == 0 || total_tokens(p) == 0) return GDR_OK;
     return from_cuda(gdr::launch_mixed_tc_noalloc(p, q, k, v, g, beta, state_pool, state_slots,
                                                   n_slots, out, static_cast<cudaStream_t>(stream)));
+}
+
+gdr_status gdr_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+    if (limit_ns <= 0 || limit_ns > 100000000) return GDR_ERR_INVALID;  // at most 0.1 s
+    return from_cuda(gdr::launch_selftest_wait(static_cast<uint64_t>(limit_ns),
+                                               static_cast<cudaStream_t>(stream)));
 }
 
 gdr_status gdr_device_error(void) {

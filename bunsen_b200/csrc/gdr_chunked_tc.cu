@@ -1000,6 +1000,23 @@ bool make_map(CUtensorMap* map, const void* base, int64_t tokens, int heads) {
 
 }  // namespace
 
+// A self-test of the bounded waits: one thread waits, at most `limit_ns`, for
+// an mbarrier phase that nothing completes, with the same wait the kernels
+// use; when the wait gives up it records the failure exactly as they do.
+__global__ void selftest_wait(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (!mbar_wait(&bar, 0, limit_ns)) atomicOr(&g_tc_error, 1);
+    mbar_inval(&bar);
+}
+
+cudaError_t launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream) {
+    selftest_wait<<<1, 32, 0, stream>>>(limit_ns);
+    return cudaGetLastError();
+}
+
 // Reads and clears the record of a bounded wait that ran out.
 cudaError_t take_device_error(int* flag) {
     cudaError_t e = cudaMemcpyFromSymbol(flag, g_tc_error, sizeof(int));

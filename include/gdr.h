@@ -167,6 +167,13 @@ gdr_status gdr_mixed_noalloc(const gdr_params* params, const void* q, const void
  * else GDR_OK. Synchronous: waits for the device's outstanding work. */
 gdr_status gdr_device_error(void);
 
+/* A self-test of failure detection: launches one thread that waits, at most
+ * `limit_ns` (0 < limit_ns <= 1e8, else GDR_ERR_INVALID), for a device-side
+ * barrier nothing completes, through the same bounded wait the kernels use.
+ * The wait gives up, the kernel returns, and the next gdr_device_error()
+ * reports GDR_ERR_TIMEOUT; the context stays usable. */
+gdr_status gdr_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 /* A short English description of a status. */
 const char* gdr_status_string(gdr_status status);
 
