@@ -304,8 +304,9 @@ def bench_prefill(name: str, args, dist, dev, stream, pk, pk_kind, e2e=False, ve
     with Clocks(dist.local) as clk:
         total_ms, per = timed(step, args.steps, args.warmup, dist, stream)
     ms = total_ms / args.steps
+    launches = rule.chunked_launches(x["q"], x["v"], x.get("cu_seqlens"))
     res = {"tokens": w.tokens, "ms_per_step": ms, "value": w.tokens / (ms * 1e-3),
-           "unit": "tokens/s", "clocks": clk.summary(), "gpu_launches": args.steps,
+           "unit": "tokens/s", "clocks": clk.summary(), "gpu_launches": args.steps * launches,
            "roofline": roofline(prefill_flops(w, hv), prefill_bytes(w, hq, hv),
                                 statistics.mean(per), pk, pk_kind,
                                 measured_traffic(w.tokens * hv))}
@@ -318,7 +319,12 @@ def bench_prefill(name: str, args, dist, dev, stream, pk, pk_kind, e2e=False, ve
         if dist.rank == 0:
             o1, s1 = rule.chunked(full["q"], full["k"], full["v"], full["g"], full["beta"],
                                   full.get("state"), cu_seqlens=full.get("cu_seqlens"))
-            res["verified"] = bool(torch.equal(o_all, o1) and torch.equal(s_all, s1))
+            # Per GPU the call may cut long sequences into segments (fewer
+            # heads, fewer CTAs to fill), so the check is the bf16 tolerance.
+            eo = ((o_all.float() - o1.float()).abs().max() / o1.float().abs().max()).item()
+            es = ((s_all - s1).abs().max() / s1.abs().max()).item()
+            res["verified"] = bool(eo <= 2e-2 and es <= 1e-2)
+            res["verify_rel_err"] = {"out": eo, "state": es}
     del full
     if e2e:
         res["e2e"] = bench_e2e(w, x, rule, out, st_out, args, dist, dev, stream)

@@ -16,7 +16,7 @@ GDR_OK, GDR_ERR_INVALID, GDR_ERR_UNSUPPORTED, GDR_ERR_CUDA, GDR_ERR_TIMEOUT = ra
 GDR_ERR_CAPACITY = 5
 GDR_MIXED_NOALLOC_MAX_SEQS = 16384
 GDR_DTYPE_F32, GDR_DTYPE_BF16 = 0, 1
-GDR_ALGO_AUTO, GDR_ALGO_CUDA_CORE, GDR_ALGO_TENSOR = 0, 1, 2
+GDR_ALGO_AUTO, GDR_ALGO_CUDA_CORE, GDR_ALGO_TENSOR, GDR_ALGO_TENSOR_SPLIT = 0, 1, 2, 3
 
 # Every function include/gdr.h declares, with its ctypes signature.
 _vp, _i32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
@@ -38,6 +38,7 @@ class GdrParams(ctypes.Structure):
         ("l2norm_eps", ctypes.c_double),
         ("dtype", ctypes.c_int32),
         ("algo", ctypes.c_int32),
+        ("split_chunks", ctypes.c_int32),
     ]
 
 
@@ -45,6 +46,7 @@ _RULE_ARGS = [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
 SIGNATURES = {
     "gdr_recurrent": (_i32, _RULE_ARGS),
     "gdr_chunked": (_i32, _RULE_ARGS),
+    "gdr_chunked_launches": (_i32, [ctypes.POINTER(GdrParams), _i32]),
     "gdr_mixed_workspace_size": (_sz, [ctypes.POINTER(GdrParams)]),
     "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                          _vp, _vp, _vp, _sz, _vp]),

@@ -17,6 +17,10 @@ bool chunked_tc_supports(const gdr_params& p);
 cudaError_t launch_chunked_tc(const Problem&, const void*, const void*, const void*,
                               const float*, const float*, const float*, void*, float*,
                               cudaStream_t);
+bool split_may_help(const Problem& p);
+cudaError_t launch_chunked_split(const Problem&, const void*, const void*, const void*,
+                                 const float*, const float*, const float*, void*, float*, int,
+                                 cudaStream_t);
 cudaError_t take_device_error(int* flag);
 cudaError_t launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream);
 int mixed_noalloc_max_seqs();
@@ -73,6 +77,40 @@ bool io_ok(const Problem& p, const void* q, const void* k, const void* v, const 
 
 gdr_status from_cuda(cudaError_t e) { return e == cudaSuccess ? GDR_OK : GDR_ERR_CUDA; }
 
+enum class ChunkedPath { kNothing, kPassThrough, kTensor, kSplit, kCudaCore };
+
+// Which kernels a gdr_chunked call runs: the checks of everything but the
+// buffers, then the algorithm (GDR_ALGO_AUTO: the tensor-core kernels where
+// they apply -- split into segments when that may help -- else the f32 one).
+gdr_status chunked_path(const gdr_params* params, const int32_t* cu_seqlens, Problem& p,
+                        ChunkedPath& path) {
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    if (params->chunk_size <= 0) return GDR_ERR_INVALID;  // delta_rule.rs:233
+    const int algo = params->algo;
+    if (algo != GDR_ALGO_AUTO && algo != GDR_ALGO_CUDA_CORE && algo != GDR_ALGO_TENSOR &&
+        algo != GDR_ALGO_TENSOR_SPLIT)
+        return GDR_ERR_INVALID;
+    if (params->split_chunks < 0) return GDR_ERR_INVALID;
+    const bool tc_ok = gdr::chunked_tc_supports(*params);
+    const bool ffma_ok = gdr::chunked_ffma_supports(p.d_k, p.d_v, p.chunk);
+    if (algo == GDR_ALGO_TENSOR || algo == GDR_ALGO_TENSOR_SPLIT) {
+        if (!tc_ok) return GDR_ERR_UNSUPPORTED;
+        path = algo == GDR_ALGO_TENSOR ? ChunkedPath::kTensor : ChunkedPath::kSplit;
+    } else if (algo == GDR_ALGO_CUDA_CORE) {
+        if (!ffma_ok) return GDR_ERR_UNSUPPORTED;
+        path = ChunkedPath::kCudaCore;
+    } else {
+        if (!tc_ok && !ffma_ok) return GDR_ERR_UNSUPPORTED;
+        path = !tc_ok ? ChunkedPath::kCudaCore
+               : (params->split_chunks > 0 || gdr::split_may_help(p)) ? ChunkedPath::kSplit
+                                                                       : ChunkedPath::kTensor;
+    }
+    if (p.n_seqs == 0) path = ChunkedPath::kNothing;
+    else if (total_tokens(p) == 0) path = ChunkedPath::kPassThrough;
+    return GDR_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -94,35 +132,40 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
                        const float* g, const float* beta, const float* state_in, void* out,
                        float* state_out, const int32_t* cu_seqlens, void* stream) {
     Problem p;
-    gdr_status st = make_problem(params, cu_seqlens, p);
+    ChunkedPath path;
+    gdr_status st = chunked_path(params, cu_seqlens, p, path);
     if (st != GDR_OK) return st;
-    if (params->chunk_size <= 0) return GDR_ERR_INVALID;  // delta_rule.rs:233
     if (!io_ok(p, q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
-    const int algo = params->algo;
-    if (algo != GDR_ALGO_AUTO && algo != GDR_ALGO_CUDA_CORE && algo != GDR_ALGO_TENSOR)
-        return GDR_ERR_INVALID;
-    const bool tc_ok = gdr::chunked_tc_supports(*params);
-    const bool ffma_ok = gdr::chunked_ffma_supports(p.d_k, p.d_v, p.chunk);
-    bool use_tc;
-    if (algo == GDR_ALGO_TENSOR) {
-        if (!tc_ok) return GDR_ERR_UNSUPPORTED;
-        use_tc = true;
-    } else if (algo == GDR_ALGO_CUDA_CORE) {
-        if (!ffma_ok) return GDR_ERR_UNSUPPORTED;
-        use_tc = false;
-    } else {
-        if (!tc_ok && !ffma_ok) return GDR_ERR_UNSUPPORTED;
-        use_tc = tc_ok;
-    }
-    if (p.n_seqs == 0) return GDR_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (total_tokens(p) == 0)  // nothing to run: the state passes through
-        return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out,
-                                               state_out, s));
-    if (use_tc)
-        return from_cuda(gdr::launch_chunked_tc(p, q, k, v, g, beta, state_in, out, state_out, s));
+    switch (path) {
+        case ChunkedPath::kNothing:
+            return GDR_OK;
+        case ChunkedPath::kPassThrough:  // no tokens: the state passes through
+            return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in,
+                                                   out, state_out, s));
+        case ChunkedPath::kSplit:
+            return from_cuda(gdr::launch_chunked_split(p, q, k, v, g, beta, state_in, out,
+                                                       state_out, params->split_chunks, s));
+        case ChunkedPath::kTensor:
+            return from_cuda(
+                gdr::launch_chunked_tc(p, q, k, v, g, beta, state_in, out, state_out, s));
+        case ChunkedPath::kCudaCore:
+            break;
+    }
     return from_cuda(gdr::launch_chunked_ffma(p, params->dtype, q, k, v, g, beta, state_in, out,
                                               state_out, s));
+}
+
+int32_t gdr_chunked_launches(const gdr_params* params, int32_t packed) {
+    const int32_t any = 0;  // stands for a cu_seqlens pointer; never read
+    Problem p;
+    ChunkedPath path;
+    if (chunked_path(params, packed ? &any : nullptr, p, path) != GDR_OK) return -1;
+    switch (path) {
+        case ChunkedPath::kNothing: return 0;
+        case ChunkedPath::kSplit: return 4;  // plan, pass A, scan, pass B
+        default: return 1;
+    }
 }
 
 size_t gdr_mixed_workspace_size(const gdr_params* params) {

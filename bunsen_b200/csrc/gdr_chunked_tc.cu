@@ -47,6 +47,7 @@
 //               staging
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gdr_common.cuh"
@@ -123,18 +124,6 @@ __device__ __forceinline__ void store_half_row_sw128(uint8_t* tile, int row, int
         v.z = pack_bf16(x[8 * c + 4], x[8 * c + 5]);
         v.w = pack_bf16(x[8 * c + 6], x[8 * c + 7]);
         *reinterpret_cast<uint4*>(base + (((c0 + c) ^ (row & 7)) << 4)) = v;
-    }
-}
-
-__device__ __forceinline__ void load2x32(uint32_t taddr, float (&x)[64]) {
-    float a[32], b[32];
-    tmem_ld32(taddr, a);
-    tmem_ld32(taddr + 32, b);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        x[i] = a[i];
-        x[32 + i] = b[i];
     }
 }
 
@@ -288,19 +277,25 @@ __device__ void unit_lower_inverse_64(uint8_t* ST, int tid, const float* fac0, c
     }
 }
 
+// Variants of an item, for the segments of a split sequence: start from the
+// identity instead of state_in; take v as zero (no V tiles, U = 0); write no
+// output (no Q tiles, no output products).
+constexpr uint32_t kItemIdentity = 1, kItemZeroV = 2, kItemNoOut = 4;
+
 // One (sequence, value head): positions [t0, t0 + len) of value head h, from
-// state_in (null: zeros; may equal state_out) to state_out, both that head's
-// [d_k, d_v] f32 state. `smem` is the CTA's 1024-aligned dynamic shared
-// memory. Allocates and frees 256 TMEM columns; `last_alloc` gives up the
-// CTA's right to allocate TMEM again, which only a CTA that runs no further
-// item may do.
+// state_in (null: zeros; may equal state_out) to state_out (null: not
+// stored), both that head's [d_k, d_v] f32 state. `smem` is the CTA's
+// 1024-aligned dynamic shared memory; `tbase` the CTA's 256 TMEM columns
+// (tmem_acquire). kFlags: kItem* above.
+template <uint32_t kFlags = 0>
 __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap* tm_q,
                                              const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                                              const float* __restrict__ g,
                                              const float* __restrict__ beta,
                                              __nv_bfloat16* __restrict__ out, int64_t t0,
                                              int64_t len, int h, const float* state_in,
-                                             float* state_out, uint8_t* smem, bool last_alloc) {
+                                             float* state_out, uint8_t* smem, uint32_t tbase) {
+    constexpr bool zero_v = kFlags & kItemZeroV, with_out = !(kFlags & kItemNoOut);
     uint8_t* KQ = smem + kOffKQ;
     uint8_t* VB = smem + kOffVB;
     uint8_t* AB = smem + kOffAB;
@@ -320,14 +315,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         ms.failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {
-        tmem_alloc(&ms.tmem_base, kTmemCols);
-        if (last_alloc) tmem_relinquish();
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tbase = ms.tmem_base;
     const uint32_t lane_addr = tbase + (static_cast<uint32_t>(qd * 32) << 16);
     // Operand descriptors; a tile offset is added to the start-address field.
     const uint64_t dKQ = sdesc_sw128(smem_u32(KQ), 16, 1024);      // K-major K, Q
@@ -338,25 +328,36 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     const uint64_t dST = sdesc_sw128(smem_u32(ST), 16, 1024);
     auto at = [](uint64_t d, uint32_t off) { return d + (off >> 4); };
 
-    auto issue_tiles = [&](int ci) {  // thread 0: chunk ci's K, Q, V tiles
+    // Thread 0: chunk ci's K, Q, V tiles (without an output, Q rows of the
+    // Gram are never read; with v zero, V is not read).
+    const uint32_t tile_tx = (2 + (with_out ? 2 : 0) + (zero_v ? 0 : 2)) * kTileBytes;
+    auto issue_tiles = [&](int ci) {
         fence_proxy_async();
-        mbar_expect_tx(&ms.bar_tma, 6 * kTileBytes);
+        mbar_expect_tx(&ms.bar_tma, tile_tx);
         const int tok = static_cast<int>(t0 + static_cast<int64_t>(ci) * kC);
         tma_load_3d(KQ + 0 * kTileBytes, tm_k, &ms.bar_tma, 0, hq, tok);
-        tma_load_3d(KQ + 1 * kTileBytes, tm_q, &ms.bar_tma, 0, hq, tok);
         tma_load_3d(KQ + 2 * kTileBytes, tm_k, &ms.bar_tma, 64, hq, tok);
-        tma_load_3d(KQ + 3 * kTileBytes, tm_q, &ms.bar_tma, 64, hq, tok);
-        tma_load_3d(VB + 0 * kTileBytes, tm_v, &ms.bar_tma, 0, h, tok);
-        tma_load_3d(VB + 1 * kTileBytes, tm_v, &ms.bar_tma, 64, h, tok);
+        if constexpr (with_out) {
+            tma_load_3d(KQ + 1 * kTileBytes, tm_q, &ms.bar_tma, 0, hq, tok);
+            tma_load_3d(KQ + 3 * kTileBytes, tm_q, &ms.bar_tma, 64, hq, tok);
+        }
+        if constexpr (!zero_v) {
+            tma_load_3d(VB + 0 * kTileBytes, tm_v, &ms.bar_tma, 0, h, tok);
+            tma_load_3d(VB + 1 * kTileBytes, tm_v, &ms.bar_tma, 64, h, tok);
+        }
     };
     auto prefetch_tiles = [&](int ci) {  // one thread: chunk ci's tiles into L2
         const int tok = static_cast<int>(t0 + static_cast<int64_t>(ci) * kC);
         tma_prefetch_3d(tm_k, 0, hq, tok);
         tma_prefetch_3d(tm_k, 64, hq, tok);
-        tma_prefetch_3d(tm_q, 0, hq, tok);
-        tma_prefetch_3d(tm_q, 64, hq, tok);
-        tma_prefetch_3d(tm_v, 0, h, tok);
-        tma_prefetch_3d(tm_v, 64, h, tok);
+        if constexpr (with_out) {
+            tma_prefetch_3d(tm_q, 0, hq, tok);
+            tma_prefetch_3d(tm_q, 64, hq, tok);
+        }
+        if constexpr (!zero_v) {
+            tma_prefetch_3d(tm_v, 0, h, tok);
+            tma_prefetch_3d(tm_v, 64, h, tok);
+        }
     };
     // Threads 0..127: chunk ci's g (tid < 64) or beta into ms.gstage by 4-byte
     // cp.async (zero-filled past the end), so no register waits for them.
@@ -402,13 +403,16 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
 
     // The initial state, transposed into TMEM: lane d holds S[:, d].
     {
+        constexpr bool identity = kFlags & kItemIdentity;
 #pragma unroll 1
         for (int cb = 0; cb < 2; ++cb) {
             float x[32];
             const int c0 = 64 * hf + 32 * cb;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                x[i] = state_in ? state_in[(c0 + i) * kD + row] : 0.f;
+                x[i] = identity   ? (c0 + i == row ? 1.f : 0.f)
+                       : state_in ? state_in[(c0 + i) * kD + row]
+                                  : 0.f;
             tmem_st32(lane_addr + kColS + c0, x);
         }
         tmem_wait_st();
@@ -532,9 +536,11 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, 64, 1, 0, 0);
+            if constexpr (!zero_v) {
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColR1, at(dVBmn, ks * 2048), at(dAB, ks * 32), id, ks > 0);
+                for (int ks = 0; ks < 4; ++ks)
+                    umma_bf16(tbase + kColR1, at(dVBmn, ks * 2048), at(dAB, ks * 32), id, ks > 0);
+            }
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tbase + kColR0, at(dKQmn, ks * 2048), at(dAB, kTileBytes + ks * 32),
@@ -570,7 +576,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
-        // (m) G3: R1 += -(S^T W^T); R0 = S^T Q^T.
+        // (m) G3: R1 += -(S^T W^T) (R1 = -(S^T W^T) when U = 0); R0 = S^T Q^T.
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id_w = idesc_bf16(128, 64, 0, 1, 1);
@@ -578,13 +584,16 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColR1, at(dST, aoff), at(dVBmn, ks * 2048), id_w, 1);
+                umma_bf16(tbase + kColR1, at(dST, aoff), at(dVBmn, ks * 2048), id_w,
+                          !zero_v || ks > 0);
             }
+            if constexpr (with_out) {
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-                const uint32_t boff = kTileBytes + (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColR0, at(dST, aoff), at(dKQ, boff), id_q, ks > 0);
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
+                    const uint32_t boff = kTileBytes + (ks >> 2) * 16384 + (ks & 3) * 32;
+                    umma_bf16(tbase + kColR0, at(dST, aoff), at(dKQ, boff), id_q, ks > 0);
+                }
             }
             umma_commit(&ms.bar_mma);
         }
@@ -616,9 +625,11 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             tc_fence_after();
             const uint32_t id4 = idesc_bf16(128, 64, 0, 0, 0);
             const uint32_t id5 = idesc_bf16(128, 128, 0, 1, 0);
+            if constexpr (with_out) {
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColR1, at(dST, ks * 32), at(dIN, ks * 32), id4, ks > 0);
+                for (int ks = 0; ks < 4; ++ks)
+                    umma_bf16(tbase + kColR1, at(dST, ks * 32), at(dIN, ks * 32), id4, ks > 0);
+            }
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
                 umma_bf16(tbase + kColS, at(dST, 16384 + ks * 32), at(dKQmn, ks * 2048), id5, 1);
@@ -631,7 +642,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         // (r) The next chunk's tiles load while this chunk's output is written.
         if (tid == 0 && ci + 1 < n_chunks) issue_tiles(ci + 1);
         // (s) O^T = (Q S)^T diag(cq) + (intra V_new)^T -> bf16 staging [t][d].
-        {
+        if constexpr (with_out) {
             float qs[32], iv[32];
             tmem_ld32(lane_addr + kColR0 + 32 * hf, qs);
             tmem_ld32(lane_addr + kColR1 + 32 * hf, iv);
@@ -663,7 +674,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         }
         tc_fence_before();
         __syncthreads();
-        {
+        if constexpr (with_out) {
             for (int e = tid; e < valid * 16; e += kThreads) {
                 const int t = e >> 4, c = e & 15;
                 const uint4* src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2) + c;
@@ -678,28 +689,53 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     // The final state, S^T lane d -> S[:, d].
     if (ok) {
         tc_fence_after();
+        if (state_out != nullptr) {
 #pragma unroll 1
-        for (int cb = 0; cb < 2; ++cb) {
-            float x[32];
-            const int c0 = 64 * hf + 32 * cb;
-            tmem_ld32(lane_addr + kColS + c0, x);
-            tmem_wait_ld();
+            for (int cb = 0; cb < 2; ++cb) {
+                float x[32];
+                const int c0 = 64 * hf + 32 * cb;
+                tmem_ld32(lane_addr + kColS + c0, x);
+                tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) state_out[(c0 + i) * kD + row] = x[i];
+                for (int i = 0; i < 32; ++i) state_out[(c0 + i) * kD + row] = x[i];
+            }
         }
     } else if (tid == 0) {
         // Give in-flight copies and MMAs a last bounded chance to land before
-        // the TMEM they target is released.
+        // the TMEM and shared memory they target are used again.
         mbar_wait(&ms.bar_mma, ph_mma, kWaitLimitNs);
         mbar_wait(&ms.bar_tma, ph_tma, kWaitLimitNs);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tbase, kTmemCols);
     if (tid == 0) {  // the barriers may be initialised again by the next item
         mbar_inval(&ms.bar_tma);
         mbar_inval(&ms.bar_mma);
     }
+}
+
+// The CTA's 256 TMEM columns, allocated once by warp 0, which then gives up
+// the CTA's right to allocate again (a CTA allocates exactly once, so the SM
+// never holds a request back); every thread gets the base address. Items
+// reuse the columns; tmem_release frees them when the CTA is done.
+__device__ __forceinline__ uint32_t tmem_acquire(uint8_t* smem) {
+    Misc& ms = *reinterpret_cast<Misc*>(smem + kOffMisc);
+    if ((threadIdx.x >> 5) == 0) {
+        tmem_alloc(&ms.tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t base = ms.tmem_base;
+    __syncthreads();
+    return base;
+}
+
+__device__ __forceinline__ void tmem_release(uint32_t tbase) {
+    tc_fence_before();
+    __syncthreads();
+    if ((threadIdx.x >> 5) == 0) tmem_dealloc(tbase, kTmemCols);
 }
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
@@ -749,8 +785,10 @@ chunked_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     int64_t t0, t1;
     seq_span(p, s, t0, t1);
     const int64_t hs = (static_cast<int64_t>(s) * p.heads_v + h) * kD * kD;
+    const uint32_t tbase = tmem_acquire(smem);
     prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, h,
-                 state_in ? state_in + hs : nullptr, state_out + hs, smem, true);
+                 state_in ? state_in + hs : nullptr, state_out + hs, smem, tbase);
+    tmem_release(tbase);
 }
 
 // The work list of a continuous batch, built in the caller's workspace:
@@ -855,6 +893,7 @@ mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = aligned_smem(smem_raw);
     __shared__ MixedItem shared_item;
+    const uint32_t tbase = tmem_acquire(smem);
     const int H = p.heads_v;
     const int n_pre_items = work[0] * H, n_dec_items = work[1] * H;
     const int first = static_cast<int>(blockIdx.x) < work[4] ? 0 : 1;  // 0: prefill, 1: decode
@@ -928,7 +967,7 @@ mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
                 int64_t t0, t1;
                 seq_span(p, it.s, t0, t1);
                 prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, t1 - t0, it.h, it.st,
-                             it.st, smem, false);
+                             it.st, smem, tbase);
                 __syncthreads();
             }
             continue;
@@ -965,6 +1004,452 @@ mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
         }
         __syncthreads();
         if (threadIdx.x == 0) mbar_inval(bar);
+        __syncthreads();
+    }
+    tmem_release(tbase);
+}
+
+// ---- Sequence-parallel prefill ----------------------------------------------
+// A (sequence, head) walks its chunks in order, so a pack whose longest
+// sequence holds more chunks than a slot's share of the work (long sequences,
+// few heads per GPU) waits on that one chain. Over positions [a, b) the
+// state update is affine in the state,
+//   S_b = M S_a + B,
+// with M (d_k x d_k) a function of k, g and beta only, and B the state that
+// the positions reach from S_a = 0. The same item run with v = 0 from S_a = I
+// ends in M (a [d_k, d_v = d_k] state); run from S_a = 0 it ends in B. A long
+// sequence therefore splits into P segments:
+//   pass A  segment 0 from the sequence's initial state (output; its final
+//           state is X_1) and, for 0 < p < P-1, the runs giving B_p and M_p
+//           (no output), beside the sequences that are not split;
+//   scan    X_{p+1} = M_p X_p + B_p in f32 on the CUDA cores;
+//   pass B  segments 1 .. P-1 from X_p (output; the last one's final state
+//           is the sequence's).
+// A middle segment runs three times, so the plan weighs the longest chain
+// against the extra work and splits nothing when the chain does not bound the
+// call.
+enum : int32_t { kRunFull = 0, kRunSeg0 = 1, kRunB = 2, kRunM = 3, kRunMid = 4, kRunLast = 5 };
+
+struct SplitDesc {
+    int32_t s;     // sequence
+    int32_t c0;    // first chunk of the segment
+    int32_t nc;    // its chunks; -1: the whole sequence
+    int32_t kind;  // kRun* | slot << 3 (the segment's index in the scratch states)
+};
+
+// Work header: [0], [1] items of pass A and pass B, [2], [3] their cursors,
+// [4] split sequences, [5] segment slots used, [6] the segment length chosen
+// (0: nothing split), [7] the scan's cursor.
+constexpr int kSplitHeader = 16;
+constexpr int kSplitCands = 16;        // segment lengths the plan tries
+// Costs in chunk-times (one chunk of one item with every CTA slot busy),
+// fitted to B200 timings of both passes and the scan at 4 to 32 value heads.
+constexpr float kItemCost = 0.5f;       // per item: state in and out, setup
+constexpr float kAloneFactor = 0.75f;   // a chunk when at most one CTA per SM is busy
+constexpr float kScanStepCost = 1.1f;   // one link of the longest scan chain
+constexpr float kScanLaunchCost = 1.0f;
+constexpr int kScanBlocks = 4;          // column blocks of a (sequence, head) scan
+
+// A pass of `n` items (`work` chunk-times in all, the longest `longest`) on
+// `slots` CTA slots, as the longest-first list schedule runs it: one wave
+// when the items fit the slots, else about half the longest beyond the
+// average load.
+__device__ __forceinline__ float pass_time(float n, float work, float longest, float slots) {
+    if (n <= 0.f) return 0.f;
+    if (n <= slots) return longest * (n <= 0.5f * slots ? kAloneFactor : 1.f);
+    return fmaxf(work / slots + 0.5f * longest, longest);
+}
+
+__device__ __forceinline__ int seg_begin(int c, int parts, int i) {
+    return static_cast<int>(static_cast<int64_t>(i) * c / parts);
+}
+
+// Exclusive prefix sum of a[0 .. 1023] in place, by a CTA of 1024 threads;
+// returns the total to every thread. `ws` holds 33 ints.
+__device__ int exclusive_scan_1024(int* a, int* ws) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int x = a[tid];
+    int inc = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) ws[w] = inc;
+    __syncthreads();
+    if (w == 0) {
+        const int t = ws[lane];
+        int it = t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, it, o);
+            if (lane >= o) it += y;
+        }
+        ws[lane] = it - t;
+        if (lane == 31) ws[32] = it;
+    }
+    __syncthreads();
+    a[tid] = inc - x + ws[w];
+    const int total = ws[32];
+    __syncthreads();
+    return total;
+}
+
+// One CTA of 1024 threads (one per length bucket). Candidate segment lengths l_min * 1.15^i (or
+// `forced` alone) are scored as
+//   max(work_A / slots, longest item of A) + max(work_B / slots, longest of B)
+// in chunk-times, against max(work / slots, longest sequence) unsplit; the
+// best one is used if it beats not splitting (`forced` is used whenever it
+// splits anything). Items of each pass are listed longest first.
+__global__ void __launch_bounds__(1024)
+plan_split(const Problem p, int32_t* work, SplitDesc* da, SplitDesc* db, int4* splits,
+           int slots, int l_min, int forced, int seg_cap) {
+    // Per candidate: work and longest item of each pass, segments, split
+    // sequences, scan steps (total and longest chain); [kSplitCands]: unsplit.
+    __shared__ float est_work_a[kSplitCands + 1], est_max_a[kSplitCands + 1],
+        est_work_b[kSplitCands], est_max_b[kSplitCands];
+    __shared__ int est_items_a[kSplitCands + 1], est_items_b[kSplitCands];
+    __shared__ int est_segs[kSplitCands], est_split[kSplitCands], est_chain[kSplitCands];
+    __shared__ int hist[3][kPlanBuckets];  // pass A items, pass B items, split sequences
+    __shared__ int chosen, n_split, n_slot;
+    __shared__ int warp_sums[33];
+    int n_a, n_b;
+    const int n = p.n_seqs, H = p.heads_v, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int n_cand = forced > 0 ? 1 : kSplitCands;
+    auto cand = [&](int i) {
+        return forced > 0 ? forced : static_cast<int>(l_min * __powf(1.15f, static_cast<float>(i)));
+    };
+    auto chunks_of = [&](int s) {
+        int64_t a, b;
+        seq_span(p, s, a, b);
+        return static_cast<int>((b - a + kC - 1) / kC);
+    };
+    auto bucket = [&](int c) {  // descending chunk count
+        return kPlanBuckets - 1 - (c < kPlanBuckets - 1 ? c : kPlanBuckets - 1);
+    };
+    for (int i = tid; i < kPlanBuckets; i += blockDim.x) hist[0][i] = hist[1][i] = hist[2][i] = 0;
+    if (tid == 0) n_split = n_slot = 0;
+    // Warp i scores candidate i (warp kSplitCands: no split), lanes over the
+    // sequences, then one warp reduction.
+    if (warp <= kSplitCands && (warp < n_cand || warp == kSplitCands)) {
+        const int L = warp < kSplitCands ? cand(warp) : 0;
+        float wa = 0.f, ma = 0.f, wb = 0.f, mb = 0.f;
+        int na = 0, nb = 0, segs = 0, nsp = 0, chain = 0;
+        for (int s = lane; s < n; s += 32) {
+            const int c = chunks_of(s);
+            const int parts = L > 0 ? (c + L - 1) / L : 1;
+            if (parts < 3) {
+                wa += c + kItemCost;
+                ma = fmaxf(ma, c + kItemCost);
+                na += 1;
+                continue;
+            }
+            // Segment sizes are floor(c / parts) or one more; the first is
+            // the floor.
+            const float first = static_cast<float>(c / parts);
+            const float last = static_cast<float>(c - seg_begin(c, parts, parts - 1));
+            const float big = static_cast<float>((c + parts - 1) / parts);
+            const float mid = static_cast<float>(c) - first - last;
+            wa += first + kItemCost + 2.f * (mid + (parts - 2) * kItemCost);
+            wb += static_cast<float>(c) - first + (parts - 1) * kItemCost;
+            ma = fmaxf(ma, big + kItemCost);
+            mb = fmaxf(mb, big + kItemCost);
+            na += 1 + 2 * (parts - 2);
+            nb += parts - 1;
+            segs += parts;
+            nsp += 1;
+            chain = max(chain, parts - 2);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            wa += __shfl_xor_sync(0xffffffffu, wa, o);
+            wb += __shfl_xor_sync(0xffffffffu, wb, o);
+            na += __shfl_xor_sync(0xffffffffu, na, o);
+            nb += __shfl_xor_sync(0xffffffffu, nb, o);
+            ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
+            mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            segs += __shfl_xor_sync(0xffffffffu, segs, o);
+            nsp += __shfl_xor_sync(0xffffffffu, nsp, o);
+            chain = max(chain, __shfl_xor_sync(0xffffffffu, chain, o));
+        }
+        if (lane == 0) {
+            est_work_a[warp] = wa;
+            est_max_a[warp] = ma;
+            est_items_a[warp] = na;
+            if (warp < kSplitCands) {
+                est_work_b[warp] = wb;
+                est_max_b[warp] = mb;
+                est_items_b[warp] = nb;
+                est_segs[warp] = segs;
+                est_split[warp] = nsp;
+                est_chain[warp] = chain;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const float fh = static_cast<float>(H), fs = static_cast<float>(slots);
+        auto pass = [&](int items, float work, float longest) {
+            return pass_time(items * fh, work * fh, longest, fs);
+        };
+        const int u = kSplitCands;
+        float best = forced > 0 ? INFINITY : pass(est_items_a[u], est_work_a[u], est_max_a[u]);
+        int best_l = 0;
+        for (int i = 0; i < n_cand; ++i) {
+            if (est_split[i] == 0 || est_segs[i] > seg_cap) continue;
+            const float est = pass(est_items_a[i], est_work_a[i], est_max_a[i]) +
+                              pass(est_items_b[i], est_work_b[i], est_max_b[i]) +
+                              kScanLaunchCost + kScanStepCost * est_chain[i];
+            if (est < best) {
+                best = est;
+                best_l = cand(i);
+            }
+        }
+        chosen = best_l;
+    }
+    __syncthreads();
+    const int L = chosen;
+    auto parts_of = [&](int c) { return L > 0 ? (c + L - 1) / L : 1; };
+    for (int s = tid; s < n; s += blockDim.x) {  // count the items by length
+        const int c = chunks_of(s), parts = parts_of(c);
+        if (parts < 3) {
+            atomicAdd(&hist[0][bucket(c)], 1);
+            continue;
+        }
+        atomicAdd(&hist[2][bucket(c)], 1);
+        for (int j = 0; j < parts; ++j) {
+            const int cs = seg_begin(c, parts, j + 1) - seg_begin(c, parts, j);
+            if (j == 0) {
+                atomicAdd(&hist[0][bucket(cs)], 1);
+            } else {
+                atomicAdd(&hist[1][bucket(cs)], 1);
+                if (j < parts - 1) atomicAdd(&hist[0][bucket(cs)], 2);
+            }
+        }
+    }
+    __syncthreads();
+    n_a = exclusive_scan_1024(hist[0], warp_sums);  // bucket counts -> cursors
+    n_b = exclusive_scan_1024(hist[1], warp_sums);
+    exclusive_scan_1024(hist[2], warp_sums);  // split sequences, longest first
+    for (int s = tid; s < n; s += blockDim.x) {  // place them
+        const int c = chunks_of(s), parts = parts_of(c);
+        if (parts < 3) {
+            da[atomicAdd(&hist[0][bucket(c)], 1)] = SplitDesc{s, 0, -1, kRunFull};
+            continue;
+        }
+        const int j = atomicAdd(&hist[2][bucket(c)], 1);
+        atomicAdd(&n_split, 1);
+        const int base = atomicAdd(&n_slot, parts);
+        splits[j] = make_int4(base, parts, s, 0);
+        for (int i = 0; i < parts; ++i) {
+            const int b0 = seg_begin(c, parts, i), cs = seg_begin(c, parts, i + 1) - b0;
+            const int slot = (base + i) << 3;
+            if (i == 0) {
+                da[atomicAdd(&hist[0][bucket(cs)], 1)] = SplitDesc{s, b0, cs, kRunSeg0 | slot};
+                continue;
+            }
+            db[atomicAdd(&hist[1][bucket(cs)], 1)] =
+                SplitDesc{s, b0, cs, (i == parts - 1 ? kRunLast : kRunMid) | slot};
+            if (i < parts - 1) {
+                const int at = atomicAdd(&hist[0][bucket(cs)], 2);
+                da[at] = SplitDesc{s, b0, cs, kRunB | slot};
+                da[at + 1] = SplitDesc{s, b0, cs, kRunM | slot};
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        work[0] = n_a;
+        work[1] = n_b;
+        work[2] = 0;
+        work[3] = 0;
+        work[4] = n_split;
+        work[5] = n_slot;
+        work[6] = L;
+        work[7] = 0;
+    }
+}
+
+// The three scratch states of a segment slot: X (the state at the segment's
+// start), B and M, each [slot][head][d_k][d_v] f32.
+__device__ __forceinline__ float* split_state(float* scratch, int seg_cap, int heads, int which,
+                                              int slot, int h) {
+    return scratch +
+           ((static_cast<int64_t>(which) * seg_cap + slot) * heads + h) * static_cast<int64_t>(kD * kD);
+}
+
+// Pass A (`which` 0) or pass B (1): CTAs pull (item, value head) pairs, the
+// value heads of one item next to each other so the two heads of a key head
+// share its tiles in L2. Each CTA holds its TMEM columns for all its items.
+__global__ void __launch_bounds__(kThreads, 2)
+split_pass(const Problem p, const __grid_constant__ CUtensorMap tm_q,
+           const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+           const float* __restrict__ g, const float* __restrict__ beta, const float* state_in,
+           __nv_bfloat16* __restrict__ out, float* state_out, int32_t* work,
+           const SplitDesc* __restrict__ desc, int which, float* scratch, int seg_cap) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = aligned_smem(smem_raw);
+    __shared__ int item;
+    const int H = p.heads_v;
+    const int n_items = work[which] * H;
+    // With fewer items than CTAs, the first CTAs (one per SM before any SM
+    // gets a second) run them and the rest leave.
+    if (static_cast<int>(blockIdx.x) >= n_items) return;
+    const uint32_t tbase = tmem_acquire(smem);
+#pragma unroll 1
+    for (;;) {
+        if (threadIdx.x == 0) item = atomicAdd(&work[2 + which], 1);
+        __syncthreads();
+        const int i = item;
+        __syncthreads();
+        if (i >= n_items) break;
+        const SplitDesc d = desc[i / H];
+        const int h = i % H;
+        int64_t a, b;
+        seq_span(p, d.s, a, b);
+        int64_t t0 = a, len = b - a;
+        if (d.nc >= 0) {
+            t0 = a + static_cast<int64_t>(d.c0) * kC;
+            const int64_t e = t0 + static_cast<int64_t>(d.nc) * kC;
+            len = (e < b ? e : b) - t0;
+        }
+        const int kind = d.kind & 7, slot = d.kind >> 3;
+        const int64_t hs = (static_cast<int64_t>(d.s) * H + h) * kD * kD;
+        const float* in = nullptr;
+        float* fin = nullptr;
+        switch (kind) {
+            case kRunFull:
+                in = state_in ? state_in + hs : nullptr;
+                fin = state_out + hs;
+                break;
+            case kRunSeg0:
+                in = state_in ? state_in + hs : nullptr;
+                fin = split_state(scratch, seg_cap, H, 0, slot + 1, h);
+                break;
+            case kRunB:
+                fin = split_state(scratch, seg_cap, H, 1, slot, h);
+                break;
+            case kRunM:
+                fin = split_state(scratch, seg_cap, H, 2, slot, h);
+                break;
+            case kRunMid:
+                in = split_state(scratch, seg_cap, H, 0, slot, h);
+                break;
+            default:  // kRunLast
+                in = split_state(scratch, seg_cap, H, 0, slot, h);
+                fin = state_out + hs;
+                break;
+        }
+        if (kind == kRunB)
+            prefill_item<kItemNoOut>(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, len, h, in, fin,
+                                     smem, tbase);
+        else if (kind == kRunM)
+            prefill_item<kItemIdentity | kItemZeroV | kItemNoOut>(
+                p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, len, h, in, fin, smem, tbase);
+        else
+            prefill_item(p, &tm_q, &tm_k, &tm_v, g, beta, out, t0, len, h, in, fin, smem, tbase);
+        __syncthreads();
+    }
+    tmem_release(tbase);
+}
+
+// X_{p+1} = M_p X_p + B_p for p = 1 .. P-2 of every split sequence and value
+// head, a block of kScanCols state columns per item (the columns of S evolve
+// independently); CTAs pull items, the longest chains first. M_p is staged
+// whole in shared memory by cp.async (every copy in flight at once), rows
+// padded to 132 floats (16-byte copies; the eight rows a warp reads fall in
+// distinct banks). Thread t accumulates rows t / 4 and t / 4 + 64, columns
+// 8 (t % 4) .. + 7 of the block, in f32.
+constexpr int kScanCols = kD / kScanBlocks;
+constexpr int kScanPad = kD + 4;
+constexpr uint32_t kScanSmem = (kD * kScanPad + kD * kScanCols) * 4;
+static_assert(kScanCols == 32, "thread layout: 64 row pairs x 4 groups of 8 columns");
+__global__ void __launch_bounds__(256, 2)
+split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H) {
+    extern __shared__ float ssm[];
+    float* Ms = ssm;
+    float* Ss = ssm + kD * kScanPad;
+    __shared__ int item;
+    const int n_items = work[4] * H * kScanBlocks;
+    if (static_cast<int>(blockIdx.x) >= n_items) return;
+    const int tid = threadIdx.x, r0 = tid >> 2, r1 = r0 + 64, cg = 8 * (tid & 3);
+    auto copy16 = [](float* dst, const float* src) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                     : "memory");
+    };
+#pragma unroll 1
+    for (;;) {
+        if (tid == 0) item = atomicAdd(&work[7], 1);
+        __syncthreads();
+        const int it = item;
+        __syncthreads();
+        if (it >= n_items) break;
+        const int cb = it % kScanBlocks, jh = it / kScanBlocks;
+        const int h = jh % H;
+        const int4 sp = splits[jh / H];
+        const int base = sp.x, parts = sp.y;
+        const int col0 = cb * kScanCols;
+        {
+            const float* x1 = split_state(scratch, seg_cap, H, 0, base + 1, h);
+            for (int e = tid; e < kD * kScanCols / 4; e += blockDim.x) {
+                const int row = e / (kScanCols / 4), c4 = e % (kScanCols / 4);
+                copy16(Ss + row * kScanCols + 4 * c4, x1 + row * kD + col0 + 4 * c4);
+            }
+        }
+#pragma unroll 1
+        for (int j = 1; j + 1 < parts; ++j) {
+            const float* m = split_state(scratch, seg_cap, H, 2, base + j, h);
+#pragma unroll
+            for (int u = 0; u < kD * kD / 4 / 256; ++u) {
+                const int e = tid + 256 * u;
+                const int row = e / (kD / 4), c = 4 * (e % (kD / 4));
+                copy16(Ms + row * kScanPad + c, m + 4 * e);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            const float* bp = split_state(scratch, seg_cap, H, 1, base + j, h) + col0 + cg;
+            float a0[8], a1[8];
+            {
+                const float4* b0 = reinterpret_cast<const float4*>(bp + r0 * kD);
+                const float4* b1 = reinterpret_cast<const float4*>(bp + r1 * kD);
+                const float4 u0 = b0[0], u1 = b0[1], w0 = b1[0], w1 = b1[1];
+                a0[0] = u0.x, a0[1] = u0.y, a0[2] = u0.z, a0[3] = u0.w;
+                a0[4] = u1.x, a0[5] = u1.y, a0[6] = u1.z, a0[7] = u1.w;
+                a1[0] = w0.x, a1[1] = w0.y, a1[2] = w0.z, a1[3] = w0.w;
+                a1[4] = w1.x, a1[5] = w1.y, a1[6] = w1.z, a1[7] = w1.w;
+            }
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            __syncthreads();
+            const float* m0 = Ms + r0 * kScanPad;
+            const float* m1 = Ms + r1 * kScanPad;
+#pragma unroll 4
+            for (int kk = 0; kk < kD; ++kk) {
+                const float x0 = m0[kk], x1 = m1[kk];
+                const float4 s0 = reinterpret_cast<const float4*>(Ss + kk * kScanCols + cg)[0];
+                const float4 s1 = reinterpret_cast<const float4*>(Ss + kk * kScanCols + cg)[1];
+                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    a0[c] = fmaf(x0, sv[c], a0[c]);
+                    a1[c] = fmaf(x1, sv[c], a1[c]);
+                }
+            }
+            __syncthreads();  // every read of Ss and Ms is done
+            float* xn = split_state(scratch, seg_cap, H, 0, base + j + 1, h) + col0 + cg;
+            const float4 o00 = make_float4(a0[0], a0[1], a0[2], a0[3]);
+            const float4 o01 = make_float4(a0[4], a0[5], a0[6], a0[7]);
+            const float4 o10 = make_float4(a1[0], a1[1], a1[2], a1[3]);
+            const float4 o11 = make_float4(a1[4], a1[5], a1[6], a1[7]);
+            reinterpret_cast<float4*>(Ss + r0 * kScanCols + cg)[0] = o00;
+            reinterpret_cast<float4*>(Ss + r0 * kScanCols + cg)[1] = o01;
+            reinterpret_cast<float4*>(Ss + r1 * kScanCols + cg)[0] = o10;
+            reinterpret_cast<float4*>(Ss + r1 * kScanCols + cg)[1] = o11;
+            reinterpret_cast<float4*>(xn + r0 * kD)[0] = o00;
+            reinterpret_cast<float4*>(xn + r0 * kD)[1] = o01;
+            reinterpret_cast<float4*>(xn + r1 * kD)[0] = o10;
+            reinterpret_cast<float4*>(xn + r1 * kD)[1] = o11;
+            __syncthreads();
+        }
         __syncthreads();
     }
 }
@@ -1133,6 +1618,124 @@ cudaError_t launch_mixed_tc_noalloc(const Problem& p, const void* q, const void*
     cudaError_t e = mixed_scratch_ptr(&work);
     if (e != cudaSuccess) return e;
     return launch_mixed_tc(p, q, k, v, g, beta, pool, slots, n_slots, out, work, stream);
+}
+
+}  // namespace gdr
+
+// ---- Sequence-parallel launch (GDR_ALGO_TENSOR_SPLIT) ----------------------
+namespace gdr {
+namespace {
+
+constexpr int kMinSegChunks = 4;
+constexpr size_t kSplitStateBudget = size_t{2} << 30;  // scratch states, bytes
+
+// The stream-ordered pool a split call's scratch comes from: one per device,
+// owned by the library, never trimmed, so repeated calls reuse its memory.
+cudaError_t split_pool(cudaMemPool_t* pool) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static cudaMemPool_t pools[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (pools[dev] == nullptr) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        if ((e = cudaMemPoolCreate(&pools[dev], &props)) != cudaSuccess) return e;
+        uint64_t keep = UINT64_MAX;
+        if ((e = cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep)) !=
+            cudaSuccess)
+            return e;
+    }
+    *pool = pools[dev];
+    return cudaSuccess;
+}
+
+// Host-side sizes of a split call: the smallest segment length the plan may
+// pick and the segment slots that bounds.
+struct SplitShape {
+    int slots;      // CTA slots (two per SM)
+    int l_min;      // chunks
+    int max_chunks; // of the longest possible sequence
+    int seg_cap;    // segment slots
+};
+
+SplitShape split_shape(const Problem& p, int forced) {
+    SplitShape sh;
+    sh.slots = 2 * sm_count();
+    const int64_t tokens = p.cu_seqlens ? p.seq_len : static_cast<int64_t>(p.n_seqs) * p.seq_len;
+    const int64_t longest = p.cu_seqlens ? tokens : p.seq_len;
+    sh.max_chunks = static_cast<int>((longest + kC - 1) / kC);
+    const int64_t chunks = p.cu_seqlens ? (tokens + kC - 1) / kC + p.n_seqs
+                                        : static_cast<int64_t>(p.n_seqs) * sh.max_chunks;
+    const double avg = static_cast<double>(chunks) * p.heads_v / sh.slots;
+    sh.l_min = forced > 0 ? forced : std::max(kMinSegChunks, static_cast<int>(0.35 * avg));
+    // A split sequence has P = ceil(c / L) >= 3 segments, so P < 1.5 c / L.
+    const int64_t cap = static_cast<int64_t>(1.6 * static_cast<double>(chunks) / sh.l_min) + 2;
+    const int64_t budget = static_cast<int64_t>(
+        kSplitStateBudget / (3 * static_cast<size_t>(p.heads_v) * kD * kD * sizeof(float)));
+    sh.seg_cap = static_cast<int>(std::max<int64_t>(3, std::min(cap, budget)));
+    return sh;
+}
+
+}  // namespace
+
+// GDR_ALGO_AUTO's choice: split when some sequence could be longer than two
+// of the shortest segments worth running.
+bool split_may_help(const Problem& p) {
+    const SplitShape sh = split_shape(p, 0);
+    return sh.max_chunks > 2 * sh.l_min;
+}
+
+cudaError_t launch_chunked_split(const Problem& p, const void* q, const void* k, const void* v,
+                                 const float* g, const float* beta, const float* state_in,
+                                 void* out, float* state_out, int forced, cudaStream_t stream) {
+    CUtensorMap mq, mk, mv;
+    cudaError_t e = make_maps(p, q, k, v, out, &mq, &mk, &mv);
+    if (e != cudaSuccess) return e;
+    if ((e = allow_smem(split_pass)) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(split_scan, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(kScanSmem))) != cudaSuccess)
+        return e;
+    const SplitShape sh = split_shape(p, forced);
+    const size_t cap_a = static_cast<size_t>(p.n_seqs) + 2 * static_cast<size_t>(sh.seg_cap);
+    const size_t cap_b = static_cast<size_t>(sh.seg_cap);
+    const size_t cap_s = static_cast<size_t>(sh.seg_cap) / 3 + 1;
+    auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    const size_t off_a = up(kSplitHeader * sizeof(int32_t));
+    const size_t off_b = off_a + up(cap_a * sizeof(SplitDesc));
+    const size_t off_s = off_b + up(cap_b * sizeof(SplitDesc));
+    const size_t off_x = off_s + up(cap_s * sizeof(int4));
+    const size_t bytes =
+        off_x + 3 * static_cast<size_t>(sh.seg_cap) * p.heads_v * kD * kD * sizeof(float);
+    cudaMemPool_t pool;
+    if ((e = split_pool(&pool)) != cudaSuccess) return e;
+    void* mem = nullptr;
+    if ((e = cudaMallocFromPoolAsync(&mem, bytes, pool, stream)) != cudaSuccess) return e;
+    uint8_t* base = static_cast<uint8_t*>(mem);
+    int32_t* work = reinterpret_cast<int32_t*>(base);
+    SplitDesc* da = reinterpret_cast<SplitDesc*>(base + off_a);
+    SplitDesc* db = reinterpret_cast<SplitDesc*>(base + off_b);
+    int4* splits = reinterpret_cast<int4*>(base + off_s);
+    float* scratch = reinterpret_cast<float*>(base + off_x);
+    auto* o = static_cast<__nv_bfloat16*>(out);
+    plan_split<<<1, 1024, 0, stream>>>(p, work, da, db, splits, sh.slots, sh.l_min, forced,
+                                       sh.seg_cap);
+    split_pass<<<sh.slots, kThreads, kSmemBytes, stream>>>(p, mq, mk, mv, g, beta, state_in, o,
+                                                          state_out, work, da, 0, scratch,
+                                                          sh.seg_cap);
+    split_scan<<<2 * sm_count(), 256, kScanSmem, stream>>>(work, splits, scratch, sh.seg_cap,
+                                                          p.heads_v);
+    split_pass<<<sh.slots, kThreads, kSmemBytes, stream>>>(p, mq, mk, mv, g, beta, state_in, o,
+                                                          state_out, work, db, 1, scratch,
+                                                          sh.seg_cap);
+    e = cudaGetLastError();
+    const cudaError_t f = cudaFreeAsync(mem, stream);
+    return e != cudaSuccess ? e : f;
 }
 
 }  // namespace gdr

@@ -26,7 +26,7 @@ from . import _lib
 
 _DTYPES = {torch.float32: _lib.GDR_DTYPE_F32, torch.bfloat16: _lib.GDR_DTYPE_BF16}
 _ALGOS = {"auto": _lib.GDR_ALGO_AUTO, "cuda_core": _lib.GDR_ALGO_CUDA_CORE,
-          "tensor": _lib.GDR_ALGO_TENSOR}
+          "tensor": _lib.GDR_ALGO_TENSOR, "tensor_split": _lib.GDR_ALGO_TENSOR_SPLIT}
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -44,7 +44,8 @@ class GatedDeltaRule:
 
     qk_l2norm_eps: float | None = 1e-6
     chunk_size: int = 64
-    algo: str = "auto"  # chunked calls: "auto", "cuda_core" or "tensor"
+    algo: str = "auto"  # chunked calls: "auto", "cuda_core", "tensor" or "tensor_split"
+    split_chunks: int = 0  # "tensor_split" / "auto": segment length in chunks, 0 = chosen
 
     def with_qk_l2norm_eps(self, eps: float | None) -> "GatedDeltaRule":
         return dataclasses.replace(self, qk_l2norm_eps=eps)
@@ -101,6 +102,12 @@ class GatedDeltaRule:
         _lib.check("gdr_mixed", status)
         return out
 
+    def chunked_launches(self, q, v, cu_seqlens=None) -> int:
+        """How many kernels ``chunked`` launches for these shapes (-1: the call
+        would be rejected)."""
+        p = self.params(q, v, cu_seqlens)
+        return _lib.load().gdr_chunked_launches(ctypes.byref(p), int(cu_seqlens is not None))
+
     # -- plumbing ------------------------------------------------------------
     def params(self, q, v, cu_seqlens) -> _lib.GdrParams:
         if cu_seqlens is None:
@@ -114,7 +121,7 @@ class GatedDeltaRule:
             d_v=v.shape[-1], chunk_size=self.chunk_size,
             use_l2norm=int(self.qk_l2norm_eps is not None),
             l2norm_eps=float(self.qk_l2norm_eps or 0.0), dtype=_DTYPES[q.dtype],
-            algo=_ALGOS[self.algo])
+            algo=_ALGOS[self.algo], split_chunks=self.split_chunks)
 
     def _run(self, fn, q, k, v, g, beta, state, cu_seqlens, out, state_out):
         packed = cu_seqlens is not None

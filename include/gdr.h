@@ -62,7 +62,7 @@
 extern "C" {
 #endif
 
-#define GDR_ABI_VERSION 1
+#define GDR_ABI_VERSION 2
 
 typedef enum gdr_status {
     GDR_OK = 0,
@@ -78,13 +78,19 @@ typedef enum gdr_dtype {
     GDR_DTYPE_BF16 = 1
 } gdr_dtype;
 
-/* Which kernel family runs a chunked call. AUTO picks the tensor-core kernel
- * for bf16, d_k = d_v = 128, chunk 64, and the CUDA-core f32 kernel
- * otherwise. */
+/* Which kernel family runs a chunked call. AUTO picks the tensor-core kernels
+ * for bf16, d_k = d_v = 128, chunk 64 -- split into segments when some
+ * sequence could be longer than twice the smallest segment worth running
+ * (see GDR_ALGO_TENSOR_SPLIT) -- and the CUDA-core f32 kernel otherwise. */
 typedef enum gdr_algo {
     GDR_ALGO_AUTO = 0,
-    GDR_ALGO_CUDA_CORE = 1, /* f32 FFMA throughout: f32 runs, any small dims */
-    GDR_ALGO_TENSOR = 2     /* tcgen05/TMEM, bf16 operands, f32 accumulate   */
+    GDR_ALGO_CUDA_CORE = 1,   /* f32 FFMA throughout: f32 runs, any small dims */
+    GDR_ALGO_TENSOR = 2,      /* tcgen05/TMEM, bf16 operands, f32 accumulate;
+                                 one pass per (sequence, head)                 */
+    GDR_ALGO_TENSOR_SPLIT = 3 /* the same kernel over segments of the long
+                                 sequences, chained by their state transitions
+                                 (sequence-parallel); allocates a stream-ordered
+                                 scratch from a library-owned pool             */
 } gdr_algo;
 
 typedef struct gdr_params {
@@ -100,6 +106,8 @@ typedef struct gdr_params {
     double l2norm_eps;  /* bunsen default 1e-6                                 */
     int32_t dtype;      /* gdr_dtype of q, k, v and out                        */
     int32_t algo;       /* gdr_algo, chunked calls only                        */
+    int32_t split_chunks; /* GDR_ALGO_TENSOR_SPLIT / AUTO: segment length in
+                             chunks; 0 lets the call choose from the lengths  */
 } gdr_params;
 
 /* The rule one position at a time (GatedDeltaRule::recurrent,
@@ -114,6 +122,12 @@ gdr_status gdr_recurrent(const gdr_params* params, const void* q, const void* k,
 gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, const void* v,
                        const float* g, const float* beta, const float* state_in, void* out,
                        float* state_out, const int32_t* cu_seqlens, void* stream);
+
+/* How many kernels a gdr_chunked call with these parameters launches (0 when
+ * there is nothing to run; 4 for the split form: plan, two passes, scan), or
+ * -1 when the call would be rejected. `packed`: the call passes cu_seqlens.
+ * No counterpart in the reference; it lets a caller count device launches. */
+int32_t gdr_chunked_launches(const gdr_params* params, int32_t packed);
 
 /* A continuous batch in one launch: the packed batch of `cu_seqlens`, whose
  * sequences of length 1 are decode rows (run as gdr_recurrent would) and whose

@@ -41,6 +41,7 @@ struct GatedDeltaRule {
     int64_t chunk_size = 64;
     gdr_dtype dtype = GDR_DTYPE_BF16;  // of q, k, v and out
     gdr_algo algo = GDR_ALGO_AUTO;
+    int32_t split_chunks = 0;  // segment length of GDR_ALGO_TENSOR_SPLIT; 0: chosen
 
     GatedDeltaRule with_qk_l2norm_eps(std::optional<double> eps) const {
         GatedDeltaRule r = *this;
@@ -109,6 +110,7 @@ struct GatedDeltaRule {
         p.l2norm_eps = qk_l2norm_eps.value_or(0.0);
         p.dtype = dtype;
         p.algo = algo;
+        p.split_chunks = split_chunks;
         const auto fn = chunked_form ? gdr_chunked : gdr_recurrent;
         const gdr_status st =
             fn(&p, q.data, k.data, v.data, static_cast<const float*>(g.data),

@@ -39,7 +39,8 @@ def test_params_layout_matches_header(tmp_path):
     src = tmp_path / "layout.c"
     src.write_text(
         '#include <stdio.h>\n#include <stddef.h>\n#include "gdr.h"\n'
-        "int main(void) { printf(\"%zu" + " %zu" * 12 + "\\n\", sizeof(gdr_params)"
+        "int main(void) { printf(\"%zu" + " %zu" * len(_lib.GdrParams._fields_)
+        + "\\n\", sizeof(gdr_params)"
         + "".join(f", offsetof(gdr_params, {f})" for f, _ in _lib.GdrParams._fields_)
         + "); return 0; }\n")
     exe = tmp_path / "layout"
@@ -53,7 +54,7 @@ def test_params_layout_matches_header(tmp_path):
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.gdr_abi_version() == 1
+    assert lib.gdr_abi_version() == 2
     for s in range(5):
         assert lib.gdr_status_string(s)
     assert lib.gdr_status_string(99) == b"unknown status"
@@ -98,3 +99,33 @@ def test_tensor_path_needs_its_shapes():
     p = _params(algo=_lib.GDR_ALGO_TENSOR)
     assert lib.gdr_chunked(ctypes.byref(p), d, d, d, d, d, None, d, d, None,
                            None) == _lib.GDR_ERR_UNSUPPORTED
+
+
+def test_split_path_needs_its_shapes_and_a_valid_length():
+    lib = _lib.load()
+    d = ctypes.c_void_p(16)
+    p = _params(algo=_lib.GDR_ALGO_TENSOR_SPLIT)
+    assert lib.gdr_chunked(ctypes.byref(p), d, d, d, d, d, None, d, d, None,
+                           None) == _lib.GDR_ERR_UNSUPPORTED
+    p = _params(split_chunks=-1)
+    assert lib.gdr_chunked(ctypes.byref(p), d, d, d, d, d, None, d, d, None,
+                           None) == _lib.GDR_ERR_INVALID
+
+
+def test_chunked_launch_counts():
+    """gdr_chunked_launches reports the kernels a call runs, without running
+    anything: one for a single-pass kernel, four for the split form (plan,
+    pass A, scan, pass B), none for an empty batch, -1 for a rejected call."""
+    lib = _lib.load()
+    n = lambda p, packed=1: lib.gdr_chunked_launches(ctypes.byref(p), packed)  # noqa: E731
+    tc = dict(d_k=128, d_v=128, chunk_size=64, dtype=_lib.GDR_DTYPE_BF16, n_seqs=64,
+              seq_len=131072)
+    assert n(_params(**tc, algo=_lib.GDR_ALGO_TENSOR)) == 1
+    assert n(_params(**tc, algo=_lib.GDR_ALGO_TENSOR_SPLIT)) == 4
+    assert n(_params(**tc, algo=_lib.GDR_ALGO_AUTO)) == 4  # a 131072-token pack may split
+    assert n(_params(**dict(tc, seq_len=64, n_seqs=1), algo=_lib.GDR_ALGO_AUTO)) == 1
+    assert n(_params(**dict(tc, n_seqs=0), algo=_lib.GDR_ALGO_AUTO)) == 0
+    assert n(_params(**dict(tc, seq_len=0), algo=_lib.GDR_ALGO_AUTO)) == 1  # state passes through
+    assert n(_params(), 0) == 1  # dense f32, d 8: the CUDA-core kernel
+    assert n(_params(chunk_size=0)) == -1
+    assert n(_params(algo=9)) == -1

@@ -78,7 +78,7 @@ def test_mixed_matches_separate_calls_at_benchmark_shape():
     w = workloads.get("mixed", scale=0.125)
     x = workloads.make_inputs(w, DEV, seed=12)
     pool = x["state"].clone()
-    rule = GatedDeltaRule()
+    rule = GatedDeltaRule(algo="tensor")  # the one-pass kernel gdr_mixed's prefill runs
     out = rule.mixed(x["q"], x["k"], x["v"], x["g"], x["beta"], pool, cu_seqlens=x["cu_seqlens"])
     n_pre = sum(1 for L in w.seqlens if L > 1)
     t_pre = sum(L for L in w.seqlens if L > 1)
