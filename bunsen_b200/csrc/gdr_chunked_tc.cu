@@ -40,11 +40,12 @@
 // Operand tiles are 128-byte swizzled; TMA writes the input tiles, the
 // CUDA-core stages write the rest with the same swizzle. Shared memory:
 //   KQ  32 KiB  [k-block][K rows 0-63 | Q rows 64-127] x 128 B  (TMA)
-//   VB  16 KiB  V (TMA) -> W^T operand
-//   AB  16 KiB  mma.sync scratch -> A diag(beta) | A diag(beta e^gamma/|k|)
+//   VB  16 KiB  V (TMA) -> W^T operand -> V_new^T operand
+//   AB  16 KiB  A diag(beta) | A diag(beta e^gamma/|k|) -> (V_new^T o r)
+//               operand
 //   IN   8 KiB  intra operand
-//   ST  36 KiB  L and A in f32 -> S^T operand -> V_new^T operands -> output
-//               staging
+//   ST  36 KiB  L (f32 diagonal blocks, bf16) and the solve's scratch -> S^T
+//               operand -> output staging
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -89,7 +90,7 @@ struct Misc {
     float rr[kC];   // e^(gamma_C - gamma_t) / |k_t|
     float cq[kC];   // e^gamma_t / (|q_t| sqrt(d_k))
     float gstage[2][kC];  // the next chunk's g and beta, landing by cp.async
-    uint64_t bar_tma, bar_mma;
+    uint64_t bar_tma, bar_mma, bar_qs;  // tiles landed; MMA groups; the (Q S)^T group
     uint32_t tmem_base;
     int failed;
 };
@@ -312,6 +313,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     if (tid == 0) {
         mbar_init(&ms.bar_tma, 1);
         mbar_init(&ms.bar_mma, 1);
+        mbar_init(&ms.bar_qs, 1);
         ms.failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -326,6 +328,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     const uint64_t dAB = sdesc_sw128(smem_u32(AB), 16, 1024);
     const uint64_t dIN = sdesc_sw128(smem_u32(IN), 16, 1024);
     const uint64_t dST = sdesc_sw128(smem_u32(ST), 16, 1024);
+    const uint64_t dVB = sdesc_sw128(smem_u32(VB), 16, 1024);       // K-major V_new^T
     auto at = [](uint64_t d, uint32_t off) { return d + (off >> 4); };
 
     // Thread 0: chunk ci's K, Q, V tiles (without an output, Q rows of the
@@ -420,7 +423,17 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     tc_fence_before();
     __syncthreads();
 
-    uint32_t ph_tma = 0, ph_mma = 0;
+    uint32_t ph_tma = 0, ph_mma = 0, ph_qs = 0;
+    auto issue_g1 = [&] {  // thread 0, once the chunk's tiles have landed
+        tc_fence_after();
+        const uint32_t id = idesc_bf16(128, 128, 0, 0, 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma_bf16(tbase + kColG, at(dKQ, off), at(dKQ, off), id, ks > 0);
+        }
+        umma_commit(&ms.bar_mma);
+    };
     bool ok = true;
     auto wait = [&](uint64_t* bar, uint32_t& ph) {
         if (!mbar_wait(bar, ph, kWaitLimitNs)) {
@@ -436,17 +449,11 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         const int64_t left = len - static_cast<int64_t>(ci) * kC;
         const int valid = static_cast<int>(left < kC ? left : kC);
         // (b)+(c) The tiles (this chunk's gates are in shared memory), then
-        //       G1: [K;Q] [K;Q]^T -> G.
-        wait(&ms.bar_tma, ph_tma);
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t id = idesc_bf16(128, 128, 0, 0, 0);
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-                umma_bf16(tbase + kColG, at(dKQ, off), at(dKQ, off), id, ks > 0);
-            }
-            umma_commit(&ms.bar_mma);
+        //       G1: [K;Q] [K;Q]^T -> G. After the first chunk, G1 was issued
+        //       at the end of the previous chunk.
+        if (ci == 0) {
+            wait(&ms.bar_tma, ph_tma);
+            if (tid == 0) issue_g1();
         }
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
@@ -576,7 +583,8 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
-        // (m) G3: R1 += -(S^T W^T) (R1 = -(S^T W^T) when U = 0); R0 = S^T Q^T.
+        // (m) G3: R1 += -(S^T W^T) (R1 = -(S^T W^T) when U = 0), committed
+        //     alone so (n) starts while R0 = S^T Q^T runs (committed to bar_qs).
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id_w = idesc_bf16(128, 64, 0, 1, 1);
@@ -587,6 +595,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 umma_bf16(tbase + kColR1, at(dST, aoff), at(dVBmn, ks * 2048), id_w,
                           !zero_v || ks > 0);
             }
+            umma_commit(&ms.bar_mma);
             if constexpr (with_out) {
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
@@ -595,16 +604,18 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                     umma_bf16(tbase + kColR0, at(dST, aoff), at(dKQ, boff), id_q, ks > 0);
                 }
             }
-            umma_commit(&ms.bar_mma);
+            umma_commit(&ms.bar_qs);
         }
         wait(&ms.bar_mma, ph_mma);
         tc_fence_after();
-        // (n) V_new^T -> bf16 operands: plain (ST) and scaled by rr (ST + 16K).
+        // (n) V_new^T -> bf16 operands: plain (VB, free since G3's first
+        //     group) and scaled by rr (AB, free since G2); ST is still read by
+        //     the (Q S)^T group.
         {
             float vn[32];
             tmem_ld32(lane_addr + kColR1 + 32 * hf, vn);
             tmem_wait_ld();
-            store_half_row_sw128(ST, row, 4 * hf, vn);
+            store_half_row_sw128(VB, row, 4 * hf, vn);
             const float4* rr4 = reinterpret_cast<const float4*>(ms.rr + 32 * hf);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
@@ -614,7 +625,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 vn[4 * c + 2] *= r.z;
                 vn[4 * c + 3] *= r.w;
             }
-            store_half_row_sw128(ST + 16384, row, 4 * hf, vn);
+            store_half_row_sw128(AB, row, 4 * hf, vn);
         }
         if (tid < 2 * kC) gates_landed();
         tc_fence_before();
@@ -628,16 +639,17 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             if constexpr (with_out) {
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
-                    umma_bf16(tbase + kColR1, at(dST, ks * 32), at(dIN, ks * 32), id4, ks > 0);
+                    umma_bf16(tbase + kColR1, at(dVB, ks * 32), at(dIN, ks * 32), id4, ks > 0);
             }
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-                umma_bf16(tbase + kColS, at(dST, 16384 + ks * 32), at(dKQmn, ks * 2048), id5, 1);
+                umma_bf16(tbase + kColS, at(dAB, ks * 32), at(dKQmn, ks * 2048), id5, 1);
             umma_commit(&ms.bar_mma);
         }
         // (p) The next chunk's gates (this chunk's are no longer read).
         if (warp == 0 && ci + 1 < n_chunks) put_gates();
         wait(&ms.bar_mma, ph_mma);
+        wait(&ms.bar_qs, ph_qs);  // done with the G4/G5 group before it
         tc_fence_after();
         // (r) The next chunk's tiles load while this chunk's output is written.
         if (tid == 0 && ci + 1 < n_chunks) issue_tiles(ci + 1);
@@ -674,6 +686,16 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         }
         tc_fence_before();
         __syncthreads();
+        // R0 and R1 have been read: the next chunk's G1 (its tiles were issued
+        // at (r)) runs while this chunk's output is stored.
+        if (ci + 1 < n_chunks) {
+            if (tid == 0) {
+                wait(&ms.bar_tma, ph_tma);
+                issue_g1();
+            } else {
+                ph_tma ^= 1u;
+            }
+        }
         if constexpr (with_out) {
             for (int e = tid; e < valid * 16; e += kThreads) {
                 const int t = e >> 4, c = e & 15;
@@ -704,6 +726,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         // Give in-flight copies and MMAs a last bounded chance to land before
         // the TMEM and shared memory they target are used again.
         mbar_wait(&ms.bar_mma, ph_mma, kWaitLimitNs);
+        mbar_wait(&ms.bar_qs, ph_qs, kWaitLimitNs);
         mbar_wait(&ms.bar_tma, ph_tma, kWaitLimitNs);
     }
     tc_fence_before();
@@ -711,6 +734,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     if (tid == 0) {  // the barriers may be initialised again by the next item
         mbar_inval(&ms.bar_tma);
         mbar_inval(&ms.bar_mma);
+        mbar_inval(&ms.bar_qs);
     }
 }
 
