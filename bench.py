@@ -332,23 +332,20 @@ def bench_prefill(name: str, args, dist, dev, stream, pk, pk_kind, e2e=False, ve
 
 
 def bench_e2e(w, x, rule, out, st_out, args, dist, dev, stream) -> dict:
-    """The same call through the public API with host buffers: each step
-    copies its inputs from pinned host memory, runs, and reads the output and
-    the final states back."""
+    """The same rule through the public host-buffer call (``gdr_chunked_host``):
+    each step copies every input from pinned host memory to the GPU, runs, and
+    copies the outputs and final states back, groups of sequences in flight so
+    the copies in, the kernels and the copies out overlap."""
     host = {k: v.to("cpu").pin_memory() for k, v in x.items()}
-    dbuf = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
     st_h = torch.empty(st_out.shape, dtype=st_out.dtype).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out_h.numel() * out_h.element_size() + st_h.numel() * st_h.element_size()
 
     def step():
-        for k, v in host.items():
-            dbuf[k].copy_(v, non_blocking=True)
-        rule.chunked(dbuf["q"], dbuf["k"], dbuf["v"], dbuf["g"], dbuf["beta"], dbuf.get("state"),
-                     cu_seqlens=dbuf.get("cu_seqlens"), out=out, state_out=st_out)
-        out_h.copy_(out, non_blocking=True)
-        st_h.copy_(st_out, non_blocking=True)
+        rule.chunked_host(host["q"], host["k"], host["v"], host["g"], host["beta"],
+                          host.get("state"), cu_seqlens=host.get("cu_seqlens"), out=out_h,
+                          state_out=st_h, device=dev, synchronize=False)
 
     k = max(1, min(args.steps, 5))
     total, _ = timed(step, k, 1, dist, stream)

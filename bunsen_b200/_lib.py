@@ -47,6 +47,7 @@ SIGNATURES = {
     "gdr_recurrent": (_i32, _RULE_ARGS),
     "gdr_chunked": (_i32, _RULE_ARGS),
     "gdr_chunked_launches": (_i32, [ctypes.POINTER(GdrParams), _i32]),
+    "gdr_chunked_host": (_i32, _RULE_ARGS),
     "gdr_mixed_workspace_size": (_sz, [ctypes.POINTER(GdrParams)]),
     "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                          _vp, _vp, _vp, _sz, _vp]),

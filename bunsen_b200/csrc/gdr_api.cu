@@ -2,6 +2,8 @@
 // shape contracts, delta_rule.rs:135-150 and :233, become GDR_ERR_INVALID),
 // then the kernel that serves the call.
 #include <cmath>
+#include <mutex>
+#include <vector>
 
 #include "gdr_common.cuh"
 
@@ -22,6 +24,7 @@ cudaError_t launch_chunked_split(const Problem&, const void*, const void*, const
                                  const float*, const float*, const float*, void*, float*, int,
                                  cudaStream_t);
 cudaError_t take_device_error(int* flag);
+cudaError_t library_pool(cudaMemPool_t* pool);
 cudaError_t launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream);
 int mixed_noalloc_max_seqs();
 cudaError_t launch_mixed_tc_noalloc(const Problem&, const void*, const void*, const void*,
@@ -111,6 +114,38 @@ gdr_status chunked_path(const gdr_params* params, const int32_t* cu_seqlens, Pro
     return GDR_OK;
 }
 
+// ---- host-buffer calls ----------------------------------------------------
+constexpr int kHostStreams = 3;  // groups in flight: copy in, run, copy out
+constexpr int kHostGroups = 16;  // groups of whole sequences per call
+
+// The worker streams of gdr_chunked_host, created once per device and kept.
+cudaError_t host_streams(cudaStream_t** out) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static cudaStream_t streams[kMaxDevices][kHostStreams] = {};
+    static bool made[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!made[dev]) {
+        for (int i = 0; i < kHostStreams; ++i)
+            if ((e = cudaStreamCreateWithFlags(&streams[dev][i], cudaStreamNonBlocking)) !=
+                cudaSuccess)
+                return e;
+        made[dev] = true;
+    }
+    *out = streams[dev];
+    return cudaSuccess;
+}
+
+// A group's cu_seqlens, counted from its first token.
+__global__ void rebase_offsets(const int32_t* cu, int32_t n1, int32_t* out) {
+    const int32_t base = cu[0];
+    for (int i = threadIdx.x; i < n1; i += blockDim.x) out[i] = cu[i] - base;
+}
+
 }  // namespace
 
 extern "C" {
@@ -166,6 +201,130 @@ int32_t gdr_chunked_launches(const gdr_params* params, int32_t packed) {
         case ChunkedPath::kSplit: return 4;  // plan, pass A, scan, pass B
         default: return 1;
     }
+}
+
+gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void* k,
+                            const void* v, const float* g, const float* beta,
+                            const float* state_in, void* out, float* state_out,
+                            const int32_t* cu_seqlens, void* stream) {
+    Problem p;
+    ChunkedPath path;
+    gdr_status st = chunked_path(params, cu_seqlens, p, path);
+    if (st != GDR_OK) return st;
+    if (!io_ok(p, q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
+    if (path == ChunkedPath::kNothing) return GDR_OK;
+    const bool packed = cu_seqlens != nullptr;
+    const int n = p.n_seqs;
+    const int64_t total = total_tokens(p);
+    // Sequence s covers tokens [first(s), first(s + 1)).
+    if (packed) {
+        if (cu_seqlens[0] != 0 || cu_seqlens[n] != total) return GDR_ERR_INVALID;
+        for (int s = 0; s < n; ++s)
+            if (cu_seqlens[s + 1] < cu_seqlens[s]) return GDR_ERR_INVALID;
+    }
+    auto first = [&](int s) -> int64_t {
+        return packed ? cu_seqlens[s] : static_cast<int64_t>(s) * p.seq_len;
+    };
+    // Groups of whole sequences of about total / kHostGroups tokens each.
+    std::vector<int> cut{0};
+    const int64_t want = (total + kHostGroups - 1) / kHostGroups;
+    for (int s = 1; s < n; ++s)
+        if (first(s) - first(cut.back()) >= want) cut.push_back(s);
+    cut.push_back(n);
+    const int groups = static_cast<int>(cut.size()) - 1;
+    int64_t max_tok = 0, max_seq = 0;
+    for (int i = 0; i < groups; ++i) {
+        max_tok = std::max<int64_t>(max_tok, first(cut[i + 1]) - first(cut[i]));
+        max_seq = std::max<int64_t>(max_seq, cut[i + 1] - cut[i]);
+    }
+    const size_t es = params->dtype == GDR_DTYPE_BF16 ? 2 : 4;
+    const size_t row_qk = static_cast<size_t>(p.heads_qk) * p.d_k * es;
+    const size_t row_v = static_cast<size_t>(p.heads_v) * p.d_v * es;
+    const size_t row_gb = static_cast<size_t>(p.heads_v) * sizeof(float);
+    const size_t one_state = static_cast<size_t>(p.heads_v) * p.d_k * p.d_v * sizeof(float);
+    auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    // One slot of device buffers per worker stream.
+    const size_t o_q = 0, o_k = o_q + up(max_tok * row_qk), o_v = o_k + up(max_tok * row_qk),
+                 o_o = o_v + up(max_tok * row_v), o_g = o_o + up(max_tok * row_v),
+                 o_b = o_g + up(max_tok * row_gb), o_s = o_b + up(max_tok * row_gb),
+                 o_c = o_s + up(max_seq * one_state), slot = o_c + up((max_seq + 1) * 4);
+    const size_t o_all = kHostStreams * slot;
+    const size_t bytes = o_all + up((static_cast<size_t>(n) + 1) * 4);
+
+    cudaStream_t caller = static_cast<cudaStream_t>(stream);
+    cudaStream_t* ws = nullptr;
+    cudaMemPool_t pool;
+    cudaError_t e = host_streams(&ws);
+    if (e == cudaSuccess) e = gdr::library_pool(&pool);
+    void* mem = nullptr;
+    if (e == cudaSuccess) e = cudaMallocFromPoolAsync(&mem, bytes, pool, caller);
+    if (e != cudaSuccess) return GDR_ERR_CUDA;
+    uint8_t* base = static_cast<uint8_t*>(mem);
+    int32_t* cu_all = reinterpret_cast<int32_t*>(base + o_all);
+    auto ok = [&](cudaError_t x) {
+        if (e == cudaSuccess) e = x;
+    };
+    if (packed)
+        ok(cudaMemcpyAsync(cu_all, cu_seqlens, (static_cast<size_t>(n) + 1) * 4,
+                           cudaMemcpyHostToDevice, caller));
+    cudaEvent_t start, done[kHostStreams];
+    ok(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
+    for (int w = 0; w < kHostStreams; ++w)
+        ok(cudaEventCreateWithFlags(&done[w], cudaEventDisableTiming));
+    ok(cudaEventRecord(start, caller));
+    for (int w = 0; w < kHostStreams; ++w) ok(cudaStreamWaitEvent(ws[w], start, 0));
+    auto h2d = [&](void* dst, const void* src, size_t len, cudaStream_t s) {
+        if (len > 0) ok(cudaMemcpyAsync(dst, src, len, cudaMemcpyHostToDevice, s));
+    };
+    auto d2h = [&](void* dst, const void* src, size_t len, cudaStream_t s) {
+        if (len > 0) ok(cudaMemcpyAsync(dst, src, len, cudaMemcpyDeviceToHost, s));
+    };
+    const auto* hq = static_cast<const uint8_t*>(q);
+    const auto* hk = static_cast<const uint8_t*>(k);
+    const auto* hv = static_cast<const uint8_t*>(v);
+    auto* ho = static_cast<uint8_t*>(out);
+    for (int i = 0; i < groups && e == cudaSuccess; ++i) {
+        const int w = i % kHostStreams;
+        cudaStream_t s = ws[w];
+        uint8_t* b = base + w * slot;
+        const int s0 = cut[i], ns = cut[i + 1] - cut[i];
+        const int64_t t0 = first(s0), nt = first(cut[i + 1]) - t0;
+        h2d(b + o_q, hq + t0 * row_qk, nt * row_qk, s);
+        h2d(b + o_k, hk + t0 * row_qk, nt * row_qk, s);
+        h2d(b + o_v, hv + t0 * row_v, nt * row_v, s);
+        h2d(b + o_g, g + t0 * p.heads_v, nt * row_gb, s);
+        h2d(b + o_b, beta + t0 * p.heads_v, nt * row_gb, s);
+        if (state_in) h2d(b + o_s, state_in + s0 * (one_state / 4), ns * one_state, s);
+        int32_t* cu = reinterpret_cast<int32_t*>(b + o_c);
+        if (packed) {
+            rebase_offsets<<<1, 256, 0, s>>>(cu_all + s0, ns + 1, cu);
+            ok(cudaGetLastError());
+        }
+        gdr_params gp = *params;
+        if (packed) {
+            gp.n_seqs = ns;
+            gp.seq_len = static_cast<int32_t>(nt);
+        } else {
+            gp.batch = ns;
+        }
+        float* ds = reinterpret_cast<float*>(b + o_s);
+        const gdr_status r =
+            gdr_chunked(&gp, b + o_q, b + o_k, b + o_v, reinterpret_cast<float*>(b + o_g),
+                        reinterpret_cast<float*>(b + o_b), state_in ? ds : nullptr, b + o_o, ds,
+                        packed ? cu : nullptr, s);
+        if (r != GDR_OK && e == cudaSuccess) e = cudaErrorLaunchFailure;
+        d2h(ho + t0 * row_v, b + o_o, nt * row_v, s);
+        d2h(state_out + s0 * (one_state / 4), ds, ns * one_state, s);
+    }
+    // The caller's stream waits for every worker; the scratch is freed after.
+    for (int w = 0; w < kHostStreams; ++w) {
+        ok(cudaEventRecord(done[w], ws[w]));
+        ok(cudaStreamWaitEvent(caller, done[w], 0));
+    }
+    const cudaError_t f = cudaFreeAsync(mem, caller);
+    cudaEventDestroy(start);
+    for (int w = 0; w < kHostStreams; ++w) cudaEventDestroy(done[w]);
+    return from_cuda(e != cudaSuccess ? e : f);
 }
 
 size_t gdr_mixed_workspace_size(const gdr_params* params) {

@@ -1653,9 +1653,12 @@ namespace {
 constexpr int kMinSegChunks = 4;
 constexpr size_t kSplitStateBudget = size_t{2} << 30;  // scratch states, bytes
 
-// The stream-ordered pool a split call's scratch comes from: one per device,
-// owned by the library, never trimmed, so repeated calls reuse its memory.
-cudaError_t split_pool(cudaMemPool_t* pool) {
+}  // namespace
+
+// The stream-ordered pool the library's scratch comes from (split calls,
+// host-buffer calls): one per device, owned by the library, never trimmed, so
+// repeated calls reuse its memory.
+cudaError_t library_pool(cudaMemPool_t* pool) {
     constexpr int kMaxDevices = 64;
     static std::mutex mu;
     static cudaMemPool_t pools[kMaxDevices] = {};
@@ -1678,6 +1681,8 @@ cudaError_t split_pool(cudaMemPool_t* pool) {
     *pool = pools[dev];
     return cudaSuccess;
 }
+
+namespace {
 
 // Host-side sizes of a split call: the smallest segment length the plan may
 // pick and the segment slots that bounds.
@@ -1737,7 +1742,7 @@ cudaError_t launch_chunked_split(const Problem& p, const void* q, const void* k,
     const size_t bytes =
         off_x + 3 * static_cast<size_t>(sh.seg_cap) * p.heads_v * kD * kD * sizeof(float);
     cudaMemPool_t pool;
-    if ((e = split_pool(&pool)) != cudaSuccess) return e;
+    if ((e = library_pool(&pool)) != cudaSuccess) return e;
     void* mem = nullptr;
     if ((e = cudaMallocFromPoolAsync(&mem, bytes, pool, stream)) != cudaSuccess) return e;
     uint8_t* base = static_cast<uint8_t*>(mem);

@@ -102,6 +102,54 @@ class GatedDeltaRule:
         _lib.check("gdr_mixed", status)
         return out
 
+    def chunked_host(self, q, k, v, g, beta, state=None, *, cu_seqlens=None, out=None,
+                     state_out=None, device=None, synchronize=True):
+        """``chunked`` on host (CPU) tensors through ``gdr_chunked_host``: groups
+        of sequences are copied to the GPU, run and copied back with copies in,
+        kernels and copies out overlapping (pin the tensors for that). Runs on
+        ``device`` (default: the current CUDA device) after the work already on
+        its current stream; ``synchronize=False`` returns before the results
+        have landed in ``out`` / ``state_out`` (wait on the stream first)."""
+        assert self.chunk_size > 0, "a chunk of at least one position"
+        packed = cu_seqlens is not None
+        lead = 1 if packed else 2
+        check_shapes(q, k, v, g, beta, state, cu_seqlens)
+        if q.dtype not in _DTYPES:
+            raise TypeError(f"q, k, v in f32 or bf16, not {q.dtype}")
+        if q.device.type != "cpu":
+            raise RuntimeError("chunked_host takes host tensors; use chunked for CUDA tensors")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else \
+            torch.device(device)
+        if not synchronize:  # the copies read the caller's tensors after return
+            ok = all(x.is_contiguous() for x in (q, k, v, g, beta)) and \
+                g.dtype == beta.dtype == torch.float32 and \
+                (state is None or (state.is_contiguous() and state.dtype == torch.float32))
+            if not ok:
+                raise ValueError("synchronize=False needs contiguous inputs, f32 g/beta/state")
+        g = g.to(torch.float32).contiguous()
+        beta = beta.to(torch.float32).contiguous()
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        n = (cu_seqlens.numel() - 1) if packed else q.shape[0]
+        h_v, d_k, d_v = v.shape[-2], q.shape[-1], v.shape[-1]
+        if out is None:
+            out = torch.empty(v.shape[:lead] + (h_v, d_v), dtype=q.dtype).pin_memory()
+        if state_out is None:
+            state_out = torch.empty((n, h_v, d_k, d_v), dtype=torch.float32).pin_memory()
+        if state is not None:
+            state = state.to(torch.float32).contiguous()
+        if packed:
+            cu_seqlens = cu_seqlens.to(dtype=torch.int32).contiguous()
+        p = self.params(q, v, cu_seqlens)
+        with torch.cuda.device(dev):
+            status = _lib.load().gdr_chunked_host(
+                ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
+                beta.data_ptr(), _ptr(state), out.data_ptr(), state_out.data_ptr(),
+                _ptr(cu_seqlens), _stream(dev))
+            _lib.check("gdr_chunked_host", status)
+            if synchronize:
+                torch.cuda.current_stream(dev).synchronize()
+        return out, state_out
+
     def chunked_launches(self, q, v, cu_seqlens=None) -> int:
         """How many kernels ``chunked`` launches for these shapes (-1: the call
         would be rejected)."""

@@ -123,6 +123,20 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
                        const float* g, const float* beta, const float* state_in, void* out,
                        float* state_out, const int32_t* cu_seqlens, void* stream);
 
+/* gdr_chunked on HOST buffers: every pointer (cu_seqlens included) is host
+ * memory, pinned for the copies to overlap. The call copies groups of whole
+ * sequences in, runs them and copies their outputs and final states out,
+ * three groups in flight on library-owned streams, so copies in, kernels and
+ * copies out overlap; device scratch comes from the library's pool. Work is
+ * ordered after earlier work on `stream` and later work on `stream` waits for
+ * it; the host buffers must stay valid (and `out` / `state_out` unread) until
+ * `stream` has passed the call. A packed batch's cu_seqlens must start at 0,
+ * not decrease and end at seq_len (T_total). No counterpart in the reference:
+ * it serves callers whose tensors live in host memory. */
+gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void* k, const void* v,
+                            const float* g, const float* beta, const float* state_in, void* out,
+                            float* state_out, const int32_t* cu_seqlens, void* stream);
+
 /* How many kernels a gdr_chunked call with these parameters launches (0 when
  * there is nothing to run; 4 for the split form: plan, two passes, scan), or
  * -1 when the call would be rejected. `packed`: the call passes cu_seqlens.

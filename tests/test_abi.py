@@ -129,3 +129,16 @@ def test_chunked_launch_counts():
     assert n(_params(), 0) == 1  # dense f32, d 8: the CUDA-core kernel
     assert n(_params(chunk_size=0)) == -1
     assert n(_params(algo=9)) == -1
+
+
+def test_host_call_rejects_malformed_offsets_before_any_copy():
+    """gdr_chunked_host reads cu_seqlens on the host: offsets that do not start
+    at 0, decrease, or miss T_total are GDR_ERR_INVALID before any CUDA call."""
+    lib = _lib.load()
+    buf = (ctypes.c_uint8 * 4096)()
+    d = ctypes.cast(buf, ctypes.c_void_p)
+    for cu in ([0, 5, 3, 8], [1, 3, 5, 8], [0, 3, 5, 7]):
+        arr = (ctypes.c_int32 * 4)(*cu)
+        p = _params(n_seqs=3, seq_len=8, batch=0)
+        assert lib.gdr_chunked_host(ctypes.byref(p), d, d, d, d, d, None, d, d,
+                                    ctypes.cast(arr, ctypes.c_void_p), None) == _lib.GDR_ERR_INVALID
