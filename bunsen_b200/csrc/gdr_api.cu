@@ -116,7 +116,10 @@ gdr_status chunked_path(const gdr_params* params, const int32_t* cu_seqlens, Pro
 
 // ---- host-buffer calls ----------------------------------------------------
 constexpr int kHostStreams = 3;  // groups in flight: copy in, run, copy out
-constexpr int kHostGroups = 16;  // groups of whole sequences per call
+#ifndef GDR_HOST_GROUPS
+#define GDR_HOST_GROUPS 16
+#endif
+constexpr int kHostGroups = GDR_HOST_GROUPS;  // groups of whole sequences per call
 
 // The worker streams of gdr_chunked_host, created once per device and kept.
 cudaError_t host_streams(cudaStream_t** out) {
