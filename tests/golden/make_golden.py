@@ -68,6 +68,17 @@ def toy_vectors(name: str) -> dict[str, np.ndarray]:
     lm = model.model.language_model
     mixer = lm.layers[0].linear_attn
     captured: dict[str, torch.Tensor] = {}
+    # The layer's other steps around the rule (gated_delta_net.rs:396-440):
+    # the short convolution's input, the gate projections, the gated norm.
+    assert mixer.causal_conv1d_fn is None and mixer.conv1d.bias is None
+    hooks = [
+        mixer.conv1d.register_forward_hook(
+            lambda m, i, o: captured.update(conv_x=i[0])),
+        mixer.in_proj_a.register_forward_hook(lambda m, i, o: captured.update(a=o)),
+        mixer.in_proj_b.register_forward_hook(lambda m, i, o: captured.update(b=o)),
+        mixer.norm.register_forward_hook(
+            lambda m, i, o: captured.update(norm_x=i[0], norm_z=i[1], norm_out=o)),
+    ]
     inner = mixer.chunk_gated_delta_rule
 
     def spy(query, key, value, g, beta, **kw):
@@ -80,6 +91,8 @@ def toy_vectors(name: str) -> dict[str, np.ndarray]:
     ids = io["input_ids"].to(torch.int64)
     with torch.no_grad():
         lm(input_ids=ids)
+    for h in hooks:
+        h.remove()
     kw = captured["kw"]
     assert kw.get("use_qk_l2norm_in_kernel") is True and kw.get("initial_state") is None
     core = io["layer0_core"].to(torch.float64)
@@ -97,6 +110,22 @@ def toy_vectors(name: str) -> dict[str, np.ndarray]:
         "core": io["layer0_core"].numpy().astype(np.float32),
         "chunk_size": np.array(64, dtype=np.int64),
         "n_key_heads": np.array(cfg["text_config"]["linear_num_key_heads"], dtype=np.int64),
+        # The steps around the rule: conv input [T, C] and kernel [C, K]
+        # (its output, after silu and the q/k/v split, is q/k/v above, q and k
+        # repeated to the value heads); the gate projections a, b [T, H_v] with
+        # A_log and dt_bias [H_v] (giving g and beta above); the gated norm's
+        # input [T * H_v, d_v], gate z, weight [d_v], epsilon and output.
+        "conv_x": f32(captured["conv_x"][0].transpose(0, 1)),
+        "conv_w": f32(mixer.conv1d.weight[:, 0, :]),
+        "a": f32(captured["a"][0]),
+        "b": f32(captured["b"][0]),
+        "a_log": f32(mixer.A_log),
+        "dt_bias": f32(mixer.dt_bias),
+        "norm_x": f32(captured["norm_x"]),
+        "norm_z": f32(captured["norm_z"]),
+        "norm_w": f32(mixer.norm.weight),
+        "norm_eps": np.array(mixer.norm.variance_epsilon, dtype=np.float64),
+        "norm_out": f32(captured["norm_out"]),
     }
 
 
