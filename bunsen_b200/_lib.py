@@ -42,12 +42,41 @@ class GdrParams(ctypes.Structure):
     ]
 
 
+class GdrConvParams(ctypes.Structure):
+    """``struct gdr_conv_params`` of include/gdr.h."""
+
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "batch", "seq_len", "n_seqs", "channels", "taps", "split0", "split1", "silu", "dtype")]
+
+
+class GdrLayerIO(ctypes.Structure):
+    """``struct gdr_layer_io`` of include/gdr.h."""
+
+    _fields_ = [
+        ("gate_a", ctypes.c_void_p),
+        ("gate_b", ctypes.c_void_p),
+        ("a_log", ctypes.c_void_p),
+        ("dt_bias", ctypes.c_void_p),
+        ("gate_dtype", ctypes.c_int32),
+        ("norm_z", ctypes.c_void_p),
+        ("norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_double),
+    ]
+
+
 _RULE_ARGS = [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+_LAYER_ARGS = [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(GdrLayerIO),
+               _vp, _vp, _vp, _vp, _vp]
 SIGNATURES = {
     "gdr_recurrent": (_i32, _RULE_ARGS),
     "gdr_chunked": (_i32, _RULE_ARGS),
     "gdr_chunked_launches": (_i32, [ctypes.POINTER(GdrParams), _i32]),
     "gdr_chunked_host": (_i32, _RULE_ARGS),
+    "gdr_chunked_layer": (_i32, _LAYER_ARGS),
+    "gdr_recurrent_layer": (_i32, _LAYER_ARGS),
+    "gdr_causal_conv1d": (_i32, [ctypes.POINTER(GdrConvParams), _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _vp, _vp, _vp]),
+    "gdr_state_reorder": (_i32, [_vp, _vp, _vp, _i32, _i32, _sz, _vp]),
     "gdr_mixed_workspace_size": (_sz, [ctypes.POINTER(GdrParams)]),
     "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                          _vp, _vp, _vp, _sz, _vp]),

@@ -24,7 +24,21 @@ cudaError_t launch_chunked_split(const Problem&, const void*, const void*, const
                                  const float*, const float*, const float*, void*, float*, int,
                                  cudaStream_t);
 cudaError_t take_device_error(int* flag);
+cudaError_t take_layer_error(int* flag);
 cudaError_t library_pool(cudaMemPool_t* pool);
+int conv_max_taps();
+cudaError_t launch_causal_conv1d(int dtype, int32_t n_seqs, int64_t tokens, int32_t seq_len,
+                                 const int32_t* cu_seqlens, int32_t channels, int32_t taps,
+                                 int32_t split0, int32_t split1, int32_t silu, const void* x,
+                                 const void* weight, const float* state_in, void* out0,
+                                 void* out1, void* out2, float* state_out, cudaStream_t s);
+cudaError_t launch_gates(int dtype, int64_t n, int heads, const void* a, const void* b,
+                         const float* a_log, const float* dt_bias, float* g, float* beta,
+                         cudaStream_t s);
+cudaError_t launch_gated_norm(int dtype, int64_t rows, int width, const void* x, const void* z,
+                              const float* weight, float eps, void* out, cudaStream_t s);
+cudaError_t launch_reorder(const void* src, void* dst, const int32_t* sources, int32_t rows,
+                           int32_t src_rows, size_t row_bytes, cudaStream_t s);
 cudaError_t launch_selftest_wait(uint64_t limit_ns, cudaStream_t stream);
 int mixed_noalloc_max_seqs();
 cudaError_t launch_mixed_tc_noalloc(const Problem&, const void*, const void*, const void*,
@@ -330,6 +344,115 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
     return from_cuda(e != cudaSuccess ? e : f);
 }
 
+gdr_status gdr_causal_conv1d(const gdr_conv_params* params, const void* x, const void* weight,
+                             const float* state_in, void* out0, void* out1, void* out2,
+                             float* state_out, const int32_t* cu_seqlens, void* stream) {
+    if (params == nullptr) return GDR_ERR_INVALID;
+    const gdr_conv_params& a = *params;
+    const int C = a.channels, K = a.taps;
+    if (C <= 0 || K < 2 || a.seq_len < 0) return GDR_ERR_INVALID;  // causal_conv.rs:47
+    if (K > gdr::conv_max_taps()) return GDR_ERR_UNSUPPORTED;
+    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16) return GDR_ERR_INVALID;
+    if (!(0 <= a.split0 && a.split0 <= a.split1 && a.split1 <= C)) return GDR_ERR_INVALID;
+    const int32_t n = cu_seqlens ? a.n_seqs : a.batch;
+    if (n < 0) return GDR_ERR_INVALID;
+    const int64_t tokens = cu_seqlens ? a.seq_len : static_cast<int64_t>(a.batch) * a.seq_len;
+    if (tokens > 0) {
+        if (x == nullptr || weight == nullptr) return GDR_ERR_INVALID;
+        if ((a.split0 > 0 && out0 == nullptr) || (a.split1 > a.split0 && out1 == nullptr) ||
+            (C > a.split1 && out2 == nullptr))
+            return GDR_ERR_INVALID;
+    }
+    if (n == 0) return GDR_OK;
+    return from_cuda(gdr::launch_causal_conv1d(
+        a.dtype, n, tokens, a.seq_len, cu_seqlens, C, K, a.split0, a.split1, a.silu != 0, x,
+        weight, state_in, out0, out1, out2, state_out, static_cast<cudaStream_t>(stream)));
+}
+
+gdr_status gdr_state_reorder(const void* src, void* dst, const int32_t* sources, int32_t rows,
+                             int32_t src_rows, size_t row_bytes, void* stream) {
+    if (rows < 0 || src_rows < 0 || row_bytes % 4 != 0) return GDR_ERR_INVALID;
+    if (rows == 0 || row_bytes == 0) return GDR_OK;
+    if (src == nullptr || dst == nullptr || sources == nullptr) return GDR_ERR_INVALID;
+    const auto* s0 = static_cast<const uint8_t*>(src);
+    const auto* d0 = static_cast<const uint8_t*>(dst);
+    const size_t sb = static_cast<size_t>(src_rows) * row_bytes,
+                 db = static_cast<size_t>(rows) * row_bytes;
+    if (d0 < s0 + sb && s0 < d0 + db) return GDR_ERR_INVALID;  // overlap
+    return from_cuda(gdr::launch_reorder(src, dst, sources, rows, src_rows, row_bytes,
+                                         static_cast<cudaStream_t>(stream)));
+}
+
+namespace {
+
+// A rule call with the layer's gates computed first (into stream-ordered
+// scratch from the library pool) and its gated norm applied to the output.
+gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, const void* k,
+                      const void* v, const float* g, const float* beta, const gdr_layer_io* io,
+                      const float* state_in, void* out, float* state_out,
+                      const int32_t* cu_seqlens, void* stream) {
+    auto rule = chunked ? gdr_chunked : gdr_recurrent;
+    if (io == nullptr || (io->gate_a == nullptr && io->norm_z == nullptr))
+        return rule(params, q, k, v, g, beta, state_in, out, state_out, cu_seqlens, stream);
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    const int64_t tokens = total_tokens(p);
+    const bool gates = io->gate_a != nullptr, norm = io->norm_z != nullptr;
+    if (gates) {
+        if (g != nullptr || beta != nullptr) return GDR_ERR_INVALID;
+        if (io->gate_dtype != GDR_DTYPE_F32 && io->gate_dtype != GDR_DTYPE_BF16)
+            return GDR_ERR_INVALID;
+        if (tokens > 0 && (io->gate_b == nullptr || io->a_log == nullptr || io->dt_bias == nullptr))
+            return GDR_ERR_INVALID;
+    }
+    if (norm && tokens > 0 && io->norm_weight == nullptr) return GDR_ERR_INVALID;
+    if (norm && !(io->norm_eps >= 0.0)) return GDR_ERR_INVALID;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* scratch = nullptr;
+    const size_t gates_n = static_cast<size_t>(tokens) * p.heads_v;
+    if (gates && gates_n > 0) {
+        cudaMemPool_t pool;
+        if (gdr::library_pool(&pool) != cudaSuccess ||
+            cudaMallocFromPoolAsync(&scratch, 2 * gates_n * sizeof(float), pool, s) != cudaSuccess)
+            return GDR_ERR_CUDA;
+        g = static_cast<const float*>(scratch);
+        beta = static_cast<const float*>(scratch) + gates_n;
+        if (gdr::launch_gates(io->gate_dtype, static_cast<int64_t>(gates_n), p.heads_v, io->gate_a,
+                              io->gate_b, io->a_log, io->dt_bias, static_cast<float*>(scratch),
+                              static_cast<float*>(scratch) + gates_n, s) != cudaSuccess)
+            st = GDR_ERR_CUDA;
+    }
+    if (st == GDR_OK)
+        st = rule(params, q, k, v, g, beta, state_in, out, state_out, cu_seqlens, stream);
+    if (st == GDR_OK && norm && tokens > 0 &&
+        gdr::launch_gated_norm(params->dtype, tokens * p.heads_v, p.d_v, out, io->norm_z,
+                               io->norm_weight, static_cast<float>(io->norm_eps), out,
+                               s) != cudaSuccess)
+        st = GDR_ERR_CUDA;
+    if (scratch != nullptr && cudaFreeAsync(scratch, s) != cudaSuccess && st == GDR_OK)
+        st = GDR_ERR_CUDA;
+    return st;
+}
+
+}  // namespace
+
+gdr_status gdr_chunked_layer(const gdr_params* params, const void* q, const void* k,
+                             const void* v, const float* g, const float* beta,
+                             const gdr_layer_io* io, const float* state_in, void* out,
+                             float* state_out, const int32_t* cu_seqlens, void* stream) {
+    return layer_call(true, params, q, k, v, g, beta, io, state_in, out, state_out, cu_seqlens,
+                      stream);
+}
+
+gdr_status gdr_recurrent_layer(const gdr_params* params, const void* q, const void* k,
+                               const void* v, const float* g, const float* beta,
+                               const gdr_layer_io* io, const float* state_in, void* out,
+                               float* state_out, const int32_t* cu_seqlens, void* stream) {
+    return layer_call(false, params, q, k, v, g, beta, io, state_in, out, state_out, cu_seqlens,
+                      stream);
+}
+
 size_t gdr_mixed_workspace_size(const gdr_params* params) {
     if (params == nullptr || params->n_seqs < 0) return 0;
     return gdr::mixed_workspace_bytes(params->n_seqs);
@@ -384,8 +507,10 @@ gdr_status gdr_selftest_wait_timeout(int64_t limit_ns, void* stream) {
 }
 
 gdr_status gdr_device_error(void) {
-    int flag = 0;
+    int flag = 0, layer = 0;
     if (gdr::take_device_error(&flag) != cudaSuccess) return GDR_ERR_CUDA;
+    if (gdr::take_layer_error(&layer) != cudaSuccess) return GDR_ERR_CUDA;
+    flag |= layer;
     if (flag & 1) return GDR_ERR_TIMEOUT;
     return (flag & 2) ? GDR_ERR_INVALID : GDR_OK;
 }

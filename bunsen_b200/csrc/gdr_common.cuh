@@ -62,4 +62,13 @@ __device__ __forceinline__ float l2_factor(const Problem& p, float sumsq) {
     return p.use_l2norm ? 1.0f / sqrtf(sumsq + p.l2norm_eps) : 1.0f;
 }
 
+// The layer's gates from its projections (gated_delta_net.rs:422-426):
+// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b), in f32.
+__device__ __forceinline__ float gate_g(float a, float a_log, float dt_bias) {
+    const float x = a + dt_bias;
+    const float sp = x > 20.f ? x : log1pf(expf(x));
+    return -expf(a_log) * sp;
+}
+__device__ __forceinline__ float gate_beta(float b) { return 1.f / (1.f + expf(-b)); }
+
 }  // namespace gdr

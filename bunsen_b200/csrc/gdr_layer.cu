@@ -1,0 +1,320 @@
+// The gated DeltaNet layer's steps around the rule (GatedDeltaNet::forward,
+// crates/public/bunsen/src/blocks/transformers/mixers/gated_delta_net.rs:
+// 396-440): the causal depthwise convolution with its silu and the q/k/v
+// split, the gate production, the gated RMS norm of the rule's output, and
+// the decode states' row reorder (linear_attention/state.rs:112-135). All of
+// them are HBM-bound elementwise or row work on the CUDA cores: coalesced
+// loads along the channel axis, f32 arithmetic, one pass over the data.
+#include <cmath>
+
+#include "gdr_common.cuh"
+
+namespace gdr {
+
+// Device-side failures of this file's kernels since the last
+// gdr_device_error: bit 1, a reorder source row outside the pool.
+__device__ int g_layer_error;
+
+cudaError_t take_layer_error(int* flag) {
+    cudaError_t e = cudaMemcpyFromSymbol(flag, g_layer_error, sizeof(int));
+    if (e != cudaSuccess || *flag == 0) return e;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_layer_error, &zero, sizeof(int));
+}
+
+namespace {
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// ---- causal depthwise convolution (causal_conv.rs:36-69) -------------------
+struct Conv {
+    int32_t n_seqs;
+    int64_t tokens;             // all positions
+    int32_t seq_len;            // dense: positions per sequence
+    const int32_t* cu_seqlens;  // nullptr: dense
+    int32_t channels, taps;     // C, K
+    int32_t split0, split1;     // output channel cuts
+    int32_t silu;
+};
+
+constexpr int kConvTokens = 64;    // positions per CTA
+constexpr int kConvThreads = 128;  // channels per CTA, one per thread
+constexpr int kMaxTaps = 8;
+
+__device__ __forceinline__ void conv_span(const Conv& p, int s, int64_t& a, int64_t& b) {
+    if (p.cu_seqlens == nullptr) {
+        a = static_cast<int64_t>(s) * p.seq_len;
+        b = a + p.seq_len;
+        return;
+    }
+    a = p.cu_seqlens[s];
+    b = p.cu_seqlens[s + 1];
+    a = a < 0 ? 0 : (a > p.tokens ? p.tokens : a);
+    b = b < a ? a : (b > p.tokens ? p.tokens : b);
+}
+
+// The sequence holding position t: the last s with start(s) <= t < end(s)
+// (empty sequences skipped), by bisection over the offsets.
+__device__ __forceinline__ int conv_seq_of(const Conv& p, int64_t t) {
+    if (p.cu_seqlens == nullptr) return static_cast<int>(t / p.seq_len);
+    int lo = 0, hi = p.n_seqs - 1;
+    while (lo < hi) {  // first s with end(s) > t
+        const int mid = (lo + hi) >> 1;
+        int64_t a, b;
+        conv_span(p, mid, a, b);
+        if (b > t) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+// One channel per thread, kConvTokens positions per CTA: each output needs
+// only the K - 1 inputs before it, so windows run independently; the history
+// at a window's (or a sequence's) start comes from x or from the state.
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvThreads)
+conv_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ weight,
+            const float* state, T* out0, T* out1, T* out2) {
+    const int c = blockIdx.x * kConvThreads + threadIdx.x;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kConvTokens;
+    if (c >= p.channels || t0 >= p.tokens) return;
+    const int C = p.channels;
+    float w[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) w[j] = to_f32(weight[static_cast<int64_t>(c) * K + j]);
+    int s = conv_seq_of(p, t0);
+    int64_t start, end;
+    conv_span(p, s, start, end);
+    // The K - 1 inputs before t0, oldest first.
+    float h[K - 1];
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+        const int64_t u = t0 - (K - 1) + i;
+        h[i] = u >= start ? to_f32(x[u * C + c])
+               : (state && start - u <= K - 1)
+                   ? state[(static_cast<int64_t>(s) * (K - 1) + (K - 1) - (start - u)) * C + c]
+                   : 0.f;
+    }
+    T* out;
+    int64_t stride;
+    int col;
+    if (c < p.split0) {
+        out = out0, stride = p.split0, col = c;
+    } else if (c < p.split1) {
+        out = out1, stride = p.split1 - p.split0, col = c - p.split0;
+    } else {
+        out = out2, stride = C - p.split1, col = c - p.split1;
+    }
+    const int64_t t1 = t0 + kConvTokens < p.tokens ? t0 + kConvTokens : p.tokens;
+    for (int64_t t = t0; t < t1; ++t) {
+        while (t >= end && s + 1 < p.n_seqs) {  // into the next sequence
+            ++s;
+            conv_span(p, s, start, end);
+#pragma unroll
+            for (int i = 0; i < K - 1; ++i)
+                h[i] = state ? state[(static_cast<int64_t>(s) * (K - 1) + i) * C + c] : 0.f;
+        }
+        const float xt = to_f32(x[t * C + c]);
+        float acc = h[0] * w[0];
+#pragma unroll
+        for (int j = 1; j < K - 1; ++j) acc = fmaf(h[j], w[j], acc);
+        acc = fmaf(xt, w[K - 1], acc);
+        if (p.silu) acc = silu_f(acc);
+        out[t * stride + col] = from_f32<T>(acc);
+#pragma unroll
+        for (int i = 0; i + 1 < K - 1; ++i) h[i] = h[i + 1];
+        h[K - 2] = xt;
+    }
+}
+
+// The next state, per (sequence, channel): the last K - 1 inputs of the
+// window [state, x], read in full before it is written (the state may be
+// updated in place).
+template <typename T>
+__global__ void conv_state_kernel(const Conv p, const T* __restrict__ x, const float* state_in,
+                                  float* state_out) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int C = p.channels, K1 = p.taps - 1;
+    if (i >= static_cast<int64_t>(p.n_seqs) * C) return;
+    const int s = static_cast<int>(i / C), c = static_cast<int>(i % C);
+    int64_t a, b;
+    conv_span(p, s, a, b);
+    const int64_t len = b - a;
+    float old[kMaxTaps - 1];
+#pragma unroll
+    for (int j = 0; j < kMaxTaps - 1; ++j)
+        old[j] = (j < K1 && state_in) ? state_in[(static_cast<int64_t>(s) * K1 + j) * C + c] : 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxTaps - 1; ++j) {
+        if (j >= K1) break;
+        const int64_t pidx = len + j;  // index into [state (K - 1), x (len)]
+        float v = 0.f;
+        if (pidx < K1) {
+#pragma unroll
+            for (int m = 0; m < kMaxTaps - 1; ++m) v = (m == pidx) ? old[m] : v;
+        } else {
+            v = to_f32(x[(a + pidx - K1) * C + c]);
+        }
+        state_out[(static_cast<int64_t>(s) * K1 + j) * C + c] = v;
+    }
+}
+
+// ---- gates (gated_delta_net.rs:422-426) ------------------------------------
+template <typename T>
+__global__ void gates_kernel(int64_t n, int heads, const T* __restrict__ a,
+                             const T* __restrict__ b, const float* __restrict__ a_log,
+                             const float* __restrict__ dt_bias, float* g, float* beta) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int h = static_cast<int>(i % heads);
+        g[i] = gate_g(to_f32(a[i]), a_log[h], dt_bias[h]);
+        beta[i] = gate_beta(to_f32(b[i]));
+    }
+}
+
+// ---- gated RMS norm (gated_delta_net.rs:439-440) ---------------------------
+// One warp per (position, head) row of `width` features; `out` may be `x`.
+template <typename T>
+__global__ void gated_norm_kernel(int64_t rows, int width, const T* x, const T* __restrict__ z,
+                                  const float* __restrict__ weight, float eps, T* out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (row >= rows) return;
+    const T* xr = x + row * width;
+    float ss = 0.f;
+    for (int i = lane; i < width; i += 32) {
+        const float v = to_f32(xr[i]);
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / width + eps);
+    for (int i = lane; i < width; i += 32) {
+        const float v = to_f32(xr[i]) * r * weight[i];
+        out[row * width + i] = from_f32<T>(v * silu_f(to_f32(z[row * width + i])));
+    }
+}
+
+// ---- state reorder (state.rs:112-135) --------------------------------------
+// dst row r <- src row sources[r]; `words` 16-byte (or 4-byte) words per row.
+template <typename W>
+__global__ void reorder_kernel(const W* __restrict__ src, W* __restrict__ dst,
+                               const int32_t* __restrict__ sources, int32_t rows,
+                               int32_t src_rows, int64_t words) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+         i < static_cast<int64_t>(rows) * words; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int32_t r = static_cast<int32_t>(i / words);
+        const int64_t w = i % words;
+        const int32_t from = sources[r];
+        if (from < 0 || from >= src_rows) {
+            if (w == 0) atomicOr(&g_layer_error, 2);
+            continue;
+        }
+        dst[static_cast<int64_t>(r) * words + w] = src[static_cast<int64_t>(from) * words + w];
+    }
+}
+
+int grid_for(int64_t n, int block) {
+    const int64_t g = (n + block - 1) / block;
+    return static_cast<int>(g < 148 * 16 ? (g > 0 ? g : 1) : 148 * 16);
+}
+
+template <typename T, int K>
+void launch_conv_k(const Conv& p, const void* x, const void* w, const float* st, void* o0,
+                   void* o1, void* o2, cudaStream_t s) {
+    const dim3 grid((p.channels + kConvThreads - 1) / kConvThreads,
+                    static_cast<unsigned>((p.tokens + kConvTokens - 1) / kConvTokens));
+    conv_kernel<T, K><<<grid, kConvThreads, 0, s>>>(
+        p, static_cast<const T*>(x), static_cast<const T*>(w), st, static_cast<T*>(o0),
+        static_cast<T*>(o1), static_cast<T*>(o2));
+}
+
+template <typename T>
+cudaError_t launch_conv_t(const Conv& p, const void* x, const void* w, const float* st_in,
+                          void* o0, void* o1, void* o2, float* st_out, cudaStream_t s) {
+    if (p.tokens > 0) {
+        switch (p.taps) {
+            case 2: launch_conv_k<T, 2>(p, x, w, st_in, o0, o1, o2, s); break;
+            case 3: launch_conv_k<T, 3>(p, x, w, st_in, o0, o1, o2, s); break;
+            case 4: launch_conv_k<T, 4>(p, x, w, st_in, o0, o1, o2, s); break;
+            case 5: launch_conv_k<T, 5>(p, x, w, st_in, o0, o1, o2, s); break;
+            case 6: launch_conv_k<T, 6>(p, x, w, st_in, o0, o1, o2, s); break;
+            case 7: launch_conv_k<T, 7>(p, x, w, st_in, o0, o1, o2, s); break;
+            case 8: launch_conv_k<T, 8>(p, x, w, st_in, o0, o1, o2, s); break;
+            default: return cudaErrorInvalidValue;
+        }
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (st_out != nullptr && p.n_seqs > 0) {
+        const int64_t n = static_cast<int64_t>(p.n_seqs) * p.channels;
+        conv_state_kernel<T><<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+            p, static_cast<const T*>(x), st_in, st_out);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int conv_max_taps() { return kMaxTaps; }
+
+cudaError_t launch_causal_conv1d(int dtype, int32_t n_seqs, int64_t tokens, int32_t seq_len,
+                                 const int32_t* cu_seqlens, int32_t channels, int32_t taps,
+                                 int32_t split0, int32_t split1, int32_t silu, const void* x,
+                                 const void* weight, const float* state_in, void* out0,
+                                 void* out1, void* out2, float* state_out, cudaStream_t s) {
+    const Conv p{n_seqs, tokens, seq_len, cu_seqlens, channels, taps, split0, split1, silu};
+    return dtype == GDR_DTYPE_BF16
+               ? launch_conv_t<__nv_bfloat16>(p, x, weight, state_in, out0, out1, out2,
+                                              state_out, s)
+               : launch_conv_t<float>(p, x, weight, state_in, out0, out1, out2, state_out, s);
+}
+
+cudaError_t launch_gates(int dtype, int64_t n, int heads, const void* a, const void* b,
+                         const float* a_log, const float* dt_bias, float* g, float* beta,
+                         cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    if (dtype == GDR_DTYPE_BF16)
+        gates_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, s>>>(
+            n, heads, static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
+            a_log, dt_bias, g, beta);
+    else
+        gates_kernel<float><<<grid_for(n, 256), 256, 0, s>>>(
+            n, heads, static_cast<const float*>(a), static_cast<const float*>(b), a_log, dt_bias,
+            g, beta);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gated_norm(int dtype, int64_t rows, int width, const void* x, const void* z,
+                              const float* weight, float eps, void* out, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+    if (dtype == GDR_DTYPE_BF16)
+        gated_norm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+            rows, width, static_cast<const __nv_bfloat16*>(x),
+            static_cast<const __nv_bfloat16*>(z), weight, eps, static_cast<__nv_bfloat16*>(out));
+    else
+        gated_norm_kernel<float><<<grid, 256, 0, s>>>(rows, width, static_cast<const float*>(x),
+                                                      static_cast<const float*>(z), weight, eps,
+                                                      static_cast<float*>(out));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reorder(const void* src, void* dst, const int32_t* sources, int32_t rows,
+                           int32_t src_rows, size_t row_bytes, cudaStream_t s) {
+    if (rows == 0 || row_bytes == 0) return cudaSuccess;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst);
+    if (row_bytes % 16 == 0 && (al & 15) == 0) {
+        const int64_t words = static_cast<int64_t>(row_bytes / 16);
+        reorder_kernel<uint4><<<grid_for(rows * words, 256), 256, 0, s>>>(
+            static_cast<const uint4*>(src), static_cast<uint4*>(dst), sources, rows, src_rows,
+            words);
+    } else {
+        const int64_t words = static_cast<int64_t>(row_bytes / 4);
+        reorder_kernel<uint32_t><<<grid_for(rows * words, 256), 256, 0, s>>>(
+            static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), sources, rows,
+            src_rows, words);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace gdr

@@ -55,15 +55,23 @@ class GatedDeltaRule:
 
     # -- the two forms -------------------------------------------------------
     def recurrent(self, q, k, v, g, beta, state=None, *, cu_seqlens=None, out=None,
-                  state_out=None):
-        """One position at a time (``delta_rule.rs:182-209``)."""
-        return self._run("gdr_recurrent", q, k, v, g, beta, state, cu_seqlens, out, state_out)
+                  state_out=None, gates=None, norm=None):
+        """One position at a time (``delta_rule.rs:182-209``). ``gates`` and
+        ``norm`` run the layer's steps around the rule (see ``chunked``)."""
+        return self._run("gdr_recurrent", q, k, v, g, beta, state, cu_seqlens, out, state_out,
+                         gates, norm)
 
     def chunked(self, q, k, v, g, beta, state=None, *, cu_seqlens=None, out=None,
-                state_out=None):
-        """``chunk_size`` positions at a time (``delta_rule.rs:223-310``)."""
+                state_out=None, gates=None, norm=None):
+        """``chunk_size`` positions at a time (``delta_rule.rs:223-310``).
+
+        ``gates=(a, b, a_log, dt_bias)``: g and beta (pass None for both) come
+        from the layer's projections (``gated_delta_net.rs:422-426``).
+        ``norm=(z, weight, eps)``: the output is the layer's gated RMS norm of
+        the rule's output (``gated_delta_net.rs:439-440``)."""
         assert self.chunk_size > 0, "a chunk of at least one position"
-        return self._run("gdr_chunked", q, k, v, g, beta, state, cu_seqlens, out, state_out)
+        return self._run("gdr_chunked", q, k, v, g, beta, state, cu_seqlens, out, state_out,
+                         gates, norm)
 
     def mixed(self, q, k, v, g, beta, state_pool, *, cu_seqlens, state_slots=None, out=None,
               workspace=None):
@@ -171,17 +179,44 @@ class GatedDeltaRule:
             l2norm_eps=float(self.qk_l2norm_eps or 0.0), dtype=_DTYPES[q.dtype],
             algo=_ALGOS[self.algo], split_chunks=self.split_chunks)
 
-    def _run(self, fn, q, k, v, g, beta, state, cu_seqlens, out, state_out):
+    def _run(self, fn, q, k, v, g, beta, state, cu_seqlens, out, state_out, gates=None,
+             norm=None):
         packed = cu_seqlens is not None
         lead = 1 if packed else 2
+        io, keep = None, []
+        if gates is not None or norm is not None:
+            io = _lib.GdrLayerIO()
+            if gates is not None:
+                if g is not None or beta is not None:
+                    raise ValueError("with gates=(a, b, a_log, dt_bias), g and beta are None")
+                a, b, a_log, dt_bias = gates
+                if a.dtype not in _DTYPES or b.dtype != a.dtype:
+                    raise TypeError("the gate projections a, b share one dtype, f32 or bf16")
+                a, b = a.contiguous(), b.contiguous()
+                a_log = a_log.to(torch.float32).contiguous()
+                dt_bias = dt_bias.to(torch.float32).contiguous()
+                keep += [a, b, a_log, dt_bias]
+                io.gate_a, io.gate_b = a.data_ptr(), b.data_ptr()
+                io.a_log, io.dt_bias = a_log.data_ptr(), dt_bias.data_ptr()
+                io.gate_dtype = _DTYPES[a.dtype]
+                g, beta = a, b  # for the shape contract only
+            if norm is not None:
+                z, weight, eps = norm
+                if tuple(z.shape) != tuple(v.shape) or z.dtype != q.dtype:
+                    raise ValueError("the norm's gate z is shaped and typed like v and out")
+                z = z.contiguous()
+                weight = weight.to(torch.float32).contiguous()
+                keep += [z, weight]
+                io.norm_z, io.norm_weight, io.norm_eps = z.data_ptr(), weight.data_ptr(), float(eps)
         check_shapes(q, k, v, g, beta, state, cu_seqlens)
         if q.dtype not in _DTYPES:
             raise TypeError(f"q, k, v in f32 or bf16, not {q.dtype}")
         dev = q.device
         if dev.type != "cuda":
             raise RuntimeError("libgdr runs on CUDA tensors only")
-        g = g.to(torch.float32).contiguous()
-        beta = beta.to(torch.float32).contiguous()
+        if gates is None:
+            g = g.to(torch.float32).contiguous()
+            beta = beta.to(torch.float32).contiguous()
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         n = (cu_seqlens.numel() - 1) if packed else q.shape[0]
         h_v, d_k, d_v = v.shape[-2], q.shape[-1], v.shape[-1]
@@ -194,6 +229,14 @@ class GatedDeltaRule:
         if packed:
             cu_seqlens = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
         p = self.params(q, v, cu_seqlens)
+        if io is not None:
+            status = getattr(_lib.load(), fn + "_layer")(
+                ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                None if gates is not None else g.data_ptr(),
+                None if gates is not None else beta.data_ptr(), ctypes.byref(io), _ptr(state),
+                out.data_ptr(), state_out.data_ptr(), _ptr(cu_seqlens), _stream(dev))
+            _lib.check(fn + "_layer", status)
+            return out, state_out
         status = getattr(_lib.load(), fn)(
             ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
             beta.data_ptr(), _ptr(state), out.data_ptr(), state_out.data_ptr(),

@@ -137,6 +137,76 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
                             const float* g, const float* beta, const float* state_in, void* out,
                             float* state_out, const int32_t* cu_seqlens, void* stream);
 
+/* ---- The layer's steps around the rule ------------------------------------
+ * GatedDeltaNet::forward (blocks/transformers/mixers/gated_delta_net.rs:396-440)
+ * runs, around the rule: a causal depthwise convolution of in_proj_qkv(x) with
+ * silu, split into q, k, v; the gates from in_proj_a(x), in_proj_b(x); and a
+ * gated RMS norm of the rule's output with in_proj_z(x). */
+
+/* The short convolution (causal_depthwise_conv1d, ops/transformers/
+ * linear_attention/causal_conv.rs:36-69): y[t, c] = sum_j w[c, j] x[t - (K-1) + j, c],
+ * the K - 1 inputs before a sequence's first position taken from its state
+ * (zeros when state_in is NULL). x is dense [B, T, C] or packed [T_total, C]
+ * (cu_seqlens); weight [C, K], oldest tap first; states [N, K - 1, C] f32,
+ * oldest first (DeltaNetState.conv, state.rs:88). Channels [0, split0) are
+ * written to out0 as [.., split0], [split0, split1) to out1, the rest to out2
+ * (the layer's q / k / v split; split0 = split1 = C writes one [.., C]
+ * output). `silu` applies the layer's activation. state_out (NULL: none) gets
+ * the last K - 1 inputs of [state, x] and may equal state_in. */
+typedef struct gdr_conv_params {
+    int32_t batch;    /* B of a dense batch; ignored when cu_seqlens != NULL */
+    int32_t seq_len;  /* T of a dense batch, or T_total of a packed one */
+    int32_t n_seqs;   /* sequences of a packed batch */
+    int32_t channels; /* C */
+    int32_t taps;     /* K, 2 to 8 */
+    int32_t split0, split1;
+    int32_t silu;
+    int32_t dtype;    /* gdr_dtype of x, weight and the outputs */
+} gdr_conv_params;
+
+gdr_status gdr_causal_conv1d(const gdr_conv_params* params, const void* x, const void* weight,
+                             const float* state_in, void* out0, void* out1, void* out2,
+                             float* state_out, const int32_t* cu_seqlens, void* stream);
+
+/* Optional inputs of a rule call that also runs the layer's gates and gated
+ * norm. gate_a != NULL: the call's g and beta must be NULL and are computed
+ * per position and value head as g = -exp(a_log[h]) softplus(a + dt_bias[h]),
+ * beta = sigmoid(b) (gated_delta_net.rs:422-426), from a, b [T, H_v] in
+ * gate_dtype and a_log, dt_bias [H_v] f32. norm_z != NULL: `out` receives
+ * rmsnorm(core) * norm_weight * silu(z) over each head's d_v features
+ * (gated_delta_net.rs:439-440, GatedNorm), core being the rule's output in q's
+ * dtype, z [T, H_v, d_v] in q's dtype, norm_weight [d_v] f32. */
+typedef struct gdr_layer_io {
+    const void* gate_a;
+    const void* gate_b;
+    const float* a_log;
+    const float* dt_bias;
+    int32_t gate_dtype;
+    const void* norm_z;
+    const float* norm_weight;
+    double norm_eps;
+} gdr_layer_io;
+
+/* gdr_chunked / gdr_recurrent with the layer's gates and gated norm (io may
+ * be NULL: the plain call). */
+gdr_status gdr_chunked_layer(const gdr_params* params, const void* q, const void* k,
+                             const void* v, const float* g, const float* beta,
+                             const gdr_layer_io* io, const float* state_in, void* out,
+                             float* state_out, const int32_t* cu_seqlens, void* stream);
+gdr_status gdr_recurrent_layer(const gdr_params* params, const void* q, const void* k,
+                               const void* v, const float* g, const float* beta,
+                               const gdr_layer_io* io, const float* state_in, void* out,
+                               float* state_out, const int32_t* cu_seqlens, void* stream);
+
+/* DeltaNetState::reorder (state.rs:112-135) on device: row r of dst becomes row
+ * sources[r] of src, for `rows` rows of row_bytes bytes (a multiple of 4);
+ * sources is device memory; src and dst must not overlap. A source outside
+ * [0, src_rows) leaves its row untouched and is reported by gdr_device_error
+ * as GDR_ERR_INVALID. Snapshots (state.rs:201-240) are plain copies of the
+ * state buffers. */
+gdr_status gdr_state_reorder(const void* src, void* dst, const int32_t* sources, int32_t rows,
+                             int32_t src_rows, size_t row_bytes, void* stream);
+
 /* How many kernels a gdr_chunked call with these parameters launches (0 when
  * there is nothing to run; 4 for the split form: plan, two passes, scan), or
  * -1 when the call would be rejected. `packed`: the call passes cu_seqlens.

@@ -1,0 +1,132 @@
+"""The layer's steps around the rule on the GPU (causal conv + silu + split,
+gates, gated norm, state reorder) against the numpy oracles of oracle/layer.py
+and against transformers' Qwen3.5 layer 0 end to end.
+
+Tolerances: 1e-4 (max |got - want| / max |want|) for f32 runs; 2e-2 for bf16
+outputs, as for the rule."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from bunsen_b200 import _lib
+from bunsen_b200.layer import causal_conv1d, state_reorder
+from bunsen_b200.rule import GatedDeltaRule
+from oracle import layer as olayer
+from tests.conftest import TOL_BF16_OUT, TOL_BF16_STATE, TOL_F32, rel_err
+from tests.test_gpu_rule import _np, _oracle, _rand_bf16
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ok():
+    torch.cuda.synchronize()
+    assert _lib.load().gdr_device_error() == _lib.GDR_OK
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("taps", [2, 4, 7])
+@pytest.mark.parametrize("with_state", [False, True])
+def test_conv_packed_against_oracle(dtype, taps, with_state):
+    gen = torch.Generator(device=DEV).manual_seed(taps)
+    lens = [300, 1, 0, 2, 131, 64, 3]
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=DEV)
+    c = 200
+    x = torch.randn(sum(lens), c, device=DEV, generator=gen).to(dtype)
+    w = (torch.randn(c, taps, device=DEV, generator=gen) * 0.5).to(dtype)
+    s0 = (torch.randn(len(lens), taps - 1, c, device=DEV, generator=gen).to(dtype).float()
+          if with_state else None)
+    (q, k, v), nxt = causal_conv1d(x, w, s0, cu_seqlens=cu, silu=True, splits=(64, 128))
+    _ok()
+    want, want_next = olayer.causal_conv1d(_np(x), _np(w), _np(s0), cu_seqlens=_np(cu).astype(
+        np.int32), activation=True)
+    got = np.concatenate([_np(q), _np(k), _np(v)], axis=1)
+    tol = TOL_F32 if dtype == torch.float32 else TOL_BF16_OUT
+    assert rel_err(got, want) < tol
+    assert np.array_equal(_np(nxt), want_next)  # the inputs themselves, exactly
+
+
+def test_conv_dense_decode_steps_in_place():
+    """One position at a time (the decode update) from the state the last
+    step left, in place, is the one-pass convolution."""
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    b, t, c, taps = 3, 9, 96, 4
+    x = torch.randn(b, t, c, device=DEV, generator=gen)
+    w = torch.randn(c, taps, device=DEV, generator=gen)
+    whole, whole_next = causal_conv1d(x, w)
+    st = torch.zeros(b, taps - 1, c, device=DEV)
+    parts = []
+    for i in range(t):
+        y, _ = causal_conv1d(x[:, i:i + 1], w, st, state_out=st)
+        parts.append(y)
+    _ok()
+    assert rel_err(_np(torch.cat(parts, 1)), _np(whole)) < TOL_F32
+    assert torch.equal(st, whole_next)
+
+
+@pytest.mark.parametrize("name", ["toy", "toy_untied"])
+def test_layer_steps_reproduce_transformers_layer0(golden, name):
+    """in_proj_qkv(x), the gate projections and z of the toy Qwen3.5's first
+    layer through our conv + silu + split, gates, rule and gated norm (all on
+    the GPU, f32) reproduce transformers' gated-norm output."""
+    d = golden[f"{name}_layer0"]
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    hk = int(d["n_key_heads"])
+    hv, dk, dv = d["v"].shape[2], d["q"].shape[3], d["v"].shape[3]
+    (q, k, v), _ = causal_conv1d(T(d["conv_x"])[None], T(d["conv_w"]), silu=True,
+                                 splits=(hk * dk, 2 * hk * dk))
+    q, k, v = q.reshape(1, -1, hk, dk), k.reshape(1, -1, hk, dk), v.reshape(1, -1, hv, dv)
+    z = T(d["norm_z"]).reshape(1, -1, hv, dv)
+    rule = GatedDeltaRule(chunk_size=int(d["chunk_size"]))
+    out, _ = rule.chunked(q, k, v, None, None, None,
+                          gates=(T(d["a"])[None], T(d["b"])[None], T(d["a_log"]), T(d["dt_bias"])),
+                          norm=(z, T(d["norm_w"]), float(d["norm_eps"])))
+    _ok()
+    assert rel_err(_np(out).reshape(-1, dv), d["norm_out"]) < TOL_F32
+
+
+@pytest.mark.parametrize("form", ["chunked", "recurrent"])
+def test_gates_and_norm_bf16_d128_against_oracle(form):
+    """bf16, d 128: the tensor-core prefill and the d-128 decode kernel with
+    the layer's gates and gated norm, against the oracle rule on the oracle's
+    gates followed by the oracle's norm."""
+    lens = [200, 1, 70] if form == "chunked" else [1] * 6
+    x = _rand_bf16(lens, state=True, seed=31)
+    gen = torch.Generator(device=DEV).manual_seed(32)
+    t = sum(lens)
+    a = torch.randn(t, 4, device=DEV, generator=gen).bfloat16()
+    b = torch.randn(t, 4, device=DEV, generator=gen).bfloat16()
+    a_log = torch.log(torch.rand(4, device=DEV, generator=gen) * 0.5 + 0.05)
+    dt_bias = torch.randn(4, device=DEV, generator=gen) * 0.1
+    z = torch.randn(t, 4, 128, device=DEV, generator=gen).bfloat16()
+    w = torch.rand(128, device=DEV, generator=gen) + 0.5
+    out, st = getattr(GatedDeltaRule(), form)(
+        x["q"], x["k"], x["v"], None, None, x["state"], cu_seqlens=x["cu_seqlens"],
+        gates=(a, b, a_log, dt_bias), norm=(z, w, 1e-6))
+    _ok()
+    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias))
+    y = dict(x, g=torch.from_numpy(g), beta=torch.from_numpy(beta))
+    core, want_st = _oracle(form, y)
+    core = _np(torch.from_numpy(core).bfloat16())  # the rule's output in q's dtype
+    want = olayer.gated_norm(core, _np(z), _np(w), 1e-6)
+    assert rel_err(_np(out), want) < TOL_BF16_OUT
+    assert rel_err(_np(st), want_st) < TOL_BF16_STATE
+
+
+def test_reorder_and_bad_source():
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    pool = torch.randn(6, 4, 16, 16, device=DEV, generator=gen)
+    conv = torch.randn(6, 3, 40, device=DEV, generator=gen)
+    src = torch.tensor([5, 5, 0, 1, 2, 3], dtype=torch.int32, device=DEV)
+    got = state_reorder(pool, src)
+    got_c = state_reorder(conv, src)
+    _ok()
+    assert torch.equal(got, pool[src.long()]) and torch.equal(got_c, conv[src.long()])
+    out = torch.zeros_like(pool)
+    state_reorder(pool, torch.tensor([0, 9, 1, 2, 3, 4], dtype=torch.int32, device=DEV), out=out)
+    torch.cuda.synchronize()
+    assert _lib.load().gdr_device_error() == _lib.GDR_ERR_INVALID
+    assert torch.count_nonzero(out[1]) == 0 and torch.equal(out[2], pool[1])
