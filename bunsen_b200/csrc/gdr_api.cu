@@ -385,8 +385,12 @@ gdr_status gdr_state_reorder(const void* src, void* dst, const int32_t* sources,
 
 namespace {
 
-// A rule call with the layer's gates computed first (into stream-ordered
-// scratch from the library pool) and its gated norm applied to the output.
+// A rule call with the layer's gates and gated norm. The tensor-core prefill
+// (single pass or split) and the recurrent kernels produce g and beta from
+// the projections as they stage them, and the tensor-core prefill and the
+// d-128 decode apply the norm as they store the output; on the other paths
+// the gates are computed first (into stream-ordered scratch from the library
+// pool) and the norm is applied to the output after the rule.
 gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, const void* k,
                       const void* v, const float* g, const float* beta, const gdr_layer_io* io,
                       const float* state_in, void* out, float* state_out,
@@ -395,7 +399,9 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
     if (io == nullptr || (io->gate_a == nullptr && io->norm_z == nullptr))
         return rule(params, q, k, v, g, beta, state_in, out, state_out, cu_seqlens, stream);
     Problem p;
-    gdr_status st = make_problem(params, cu_seqlens, p);
+    ChunkedPath path = ChunkedPath::kTensor;
+    gdr_status st = chunked ? chunked_path(params, cu_seqlens, p, path)
+                            : make_problem(params, cu_seqlens, p);
     if (st != GDR_OK) return st;
     const int64_t tokens = total_tokens(p);
     const bool gates = io->gate_a != nullptr, norm = io->norm_z != nullptr;
@@ -406,12 +412,39 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
         if (tokens > 0 && (io->gate_b == nullptr || io->a_log == nullptr || io->dt_bias == nullptr))
             return GDR_ERR_INVALID;
     }
-    if (norm && tokens > 0 && io->norm_weight == nullptr) return GDR_ERR_INVALID;
-    if (norm && !(io->norm_eps >= 0.0)) return GDR_ERR_INVALID;
+    if (norm && ((tokens > 0 && io->norm_weight == nullptr) || !(io->norm_eps >= 0.0)))
+        return GDR_ERR_INVALID;
+    const float* g_chk = gates ? static_cast<const float*>(io->gate_a) : g;
+    const float* b_chk = gates ? static_cast<const float*>(io->gate_b) : beta;
+    if (!io_ok(p, q, k, v, g_chk, b_chk, out, state_out)) return GDR_ERR_INVALID;
+    if (!chunked && (p.d_k > 256 || p.d_v > 256)) return GDR_ERR_UNSUPPORTED;
+    if (p.n_seqs == 0 || (chunked && path == ChunkedPath::kNothing)) return GDR_OK;
+    const bool tc = chunked && (path == ChunkedPath::kTensor || path == ChunkedPath::kSplit);
+    const bool d128 = p.d_k == 128 && p.d_v == 128;
+    const bool fuse_gates = gates && (tc || !chunked);
+    const bool fuse_norm = norm && (tc || (!chunked && d128));
+    // The tensor-core prefill stages 4-byte words of the projections and
+    // reads z 16 bytes at a time.
+    if (tc && fuse_gates &&
+        ((reinterpret_cast<uintptr_t>(io->gate_a) | reinterpret_cast<uintptr_t>(io->gate_b)) & 3))
+        return GDR_ERR_INVALID;
+    if (tc && fuse_norm && (reinterpret_cast<uintptr_t>(io->norm_z) & 15)) return GDR_ERR_INVALID;
+    if (fuse_gates) {
+        p.gate_a = io->gate_a;
+        p.gate_b = io->gate_b;
+        p.a_log = io->a_log;
+        p.dt_bias = io->dt_bias;
+        p.gate_bf16 = io->gate_dtype == GDR_DTYPE_BF16;
+    }
+    if (fuse_norm) {
+        p.norm_z = io->norm_z;
+        p.norm_w = io->norm_weight;
+        p.norm_eps = static_cast<float>(io->norm_eps);
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* scratch = nullptr;
     const size_t gates_n = static_cast<size_t>(tokens) * p.heads_v;
-    if (gates && gates_n > 0) {
+    if (gates && !fuse_gates && gates_n > 0) {
         cudaMemPool_t pool;
         if (gdr::library_pool(&pool) != cudaSuccess ||
             cudaMallocFromPoolAsync(&scratch, 2 * gates_n * sizeof(float), pool, s) != cudaSuccess)
@@ -423,9 +456,22 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
                               static_cast<float*>(scratch) + gates_n, s) != cudaSuccess)
             st = GDR_ERR_CUDA;
     }
-    if (st == GDR_OK)
-        st = rule(params, q, k, v, g, beta, state_in, out, state_out, cu_seqlens, stream);
-    if (st == GDR_OK && norm && tokens > 0 &&
+    if (st == GDR_OK) {
+        cudaError_t e;
+        if (!chunked || path == ChunkedPath::kPassThrough)
+            e = gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out, state_out,
+                                      s);
+        else if (path == ChunkedPath::kSplit)
+            e = gdr::launch_chunked_split(p, q, k, v, g, beta, state_in, out, state_out,
+                                          params->split_chunks, s);
+        else if (path == ChunkedPath::kTensor)
+            e = gdr::launch_chunked_tc(p, q, k, v, g, beta, state_in, out, state_out, s);
+        else
+            e = gdr::launch_chunked_ffma(p, params->dtype, q, k, v, g, beta, state_in, out,
+                                         state_out, s);
+        st = from_cuda(e);
+    }
+    if (st == GDR_OK && norm && !fuse_norm && tokens > 0 &&
         gdr::launch_gated_norm(params->dtype, tokens * p.heads_v, p.d_v, out, io->norm_z,
                                io->norm_weight, static_cast<float>(io->norm_eps), out,
                                s) != cudaSuccess)

@@ -364,11 +364,20 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     };
     // Threads 0..127: chunk ci's g (tid < 64) or beta into ms.gstage by 4-byte
     // cp.async (zero-filled past the end), so no register waits for them.
+    // With the layer's gates fused, the 4-byte word holding the projection a
+    // (or b) is staged instead and put_gates turns it into g (or beta).
     auto stage_gates = [&](int ci) {
         const int t = tid & (kC - 1), which = tid >> 6;
         const int64_t pos = static_cast<int64_t>(ci) * kC + t;
         const int64_t at = pos < len ? pos : len - 1;
-        const float* src = (which ? beta : g) + (t0 + at) * p.heads_v + h;
+        const int64_t i = (t0 + at) * p.heads_v + h;
+        const void* src;
+        if (p.gate_a == nullptr)
+            src = (which ? beta : g) + i;
+        else if (p.gate_bf16)
+            src = static_cast<const uint8_t*>(which ? p.gate_b : p.gate_a) + ((2 * i) & ~int64_t{3});
+        else
+            src = static_cast<const float*>(which ? p.gate_b : p.gate_a) + i;
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(
                          smem_u32(&ms.gstage[which][t])),
                      "l"(src), "r"(pos < len ? 4 : 0)
@@ -376,10 +385,32 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     auto gates_landed = [] { asm volatile("cp.async.wait_group 0;" ::: "memory"); };
-    // Warp 0: the staged gates into the chunk's arrays, the log decay as its
-    // running sum (positions 2 lane, 2 lane + 1).
-    auto put_gates = [&] {
-        const float pg0 = ms.gstage[0][2 * lane], pg1 = ms.gstage[0][2 * lane + 1];
+    // Warp 0: chunk ci's staged gates into the chunk's arrays, the log decay
+    // as its running sum (positions 2 lane, 2 lane + 1). Fused gates: g and
+    // beta from the staged projections, zero past the end (as the zero-filled
+    // g and beta are).
+    auto put_gates = [&](int ci) {
+        float pg0 = ms.gstage[0][2 * lane], pg1 = ms.gstage[0][2 * lane + 1];
+        float pb0 = ms.gstage[1][2 * lane], pb1 = ms.gstage[1][2 * lane + 1];
+        if (p.gate_a != nullptr) {
+            const float al = p.a_log[h], db = p.dt_bias[h];
+            float* pg[2] = {&pg0, &pg1};
+            float* pb[2] = {&pb0, &pb1};
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int64_t pos = static_cast<int64_t>(ci) * kC + 2 * lane + u;
+                const bool in = pos < len;
+                float a = *pg[u], b = *pb[u];
+                if (p.gate_bf16) {
+                    const int64_t i = (t0 + (in ? pos : len - 1)) * p.heads_v + h;
+                    const int sh = (i & 1) ? 16 : 0;
+                    a = __uint_as_float((__float_as_uint(a) >> sh) << 16);
+                    b = __uint_as_float((__float_as_uint(b) >> sh) << 16);
+                }
+                *pg[u] = in ? gate_g(a, al, db) : 0.f;
+                *pb[u] = in ? gate_beta(b) : 0.f;
+            }
+        }
         float incl = pg0 + pg1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -391,8 +422,8 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         ms.gam[2 * lane + 1] = g1;
         ms.gl[2 * lane] = g0 * kLog2e;
         ms.gl[2 * lane + 1] = g1 * kLog2e;
-        ms.bet[2 * lane] = ms.gstage[1][2 * lane];
-        ms.bet[2 * lane + 1] = ms.gstage[1][2 * lane + 1];
+        ms.bet[2 * lane] = pb0;
+        ms.bet[2 * lane + 1] = pb1;
     };
 
     if (tid == 0 && n_chunks > 0) issue_tiles(0);
@@ -402,7 +433,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         gates_landed();
     }
     __syncthreads();
-    if (warp == 0 && n_chunks > 0) put_gates();
+    if (warp == 0 && n_chunks > 0) put_gates(0);
 
     // The initial state, transposed into TMEM: lane d holds S[:, d].
     {
@@ -647,7 +678,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             umma_commit(&ms.bar_mma);
         }
         // (p) The next chunk's gates (this chunk's are no longer read).
-        if (warp == 0 && ci + 1 < n_chunks) put_gates();
+        if (warp == 0 && ci + 1 < n_chunks) put_gates(ci + 1);
         wait(&ms.bar_mma, ph_mma);
         wait(&ms.bar_qs, ph_qs);  // done with the G4/G5 group before it
         tc_fence_after();
@@ -697,11 +728,50 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             }
         }
         if constexpr (with_out) {
-            for (int e = tid; e < valid * 16; e += kThreads) {
-                const int t = e >> 4, c = e & 15;
-                const uint4* src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2) + c;
-                uint4* dst = reinterpret_cast<uint4*>(out + ((tok0 + t) * p.heads_v + h) * kD) + c;
-                *dst = *src;
+            if (p.norm_z == nullptr) {
+                for (int e = tid; e < valid * 16; e += kThreads) {
+                    const int t = e >> 4, c = e & 15;
+                    const uint4* src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2) + c;
+                    uint4* dst =
+                        reinterpret_cast<uint4*>(out + ((tok0 + t) * p.heads_v + h) * kD) + c;
+                    *dst = *src;
+                }
+            } else {
+                // The layer's gated RMS norm of each output row: 16 lanes hold
+                // a row's 128 features (8 each) and reduce over them.
+#pragma unroll 1
+                for (int e = tid; e < kC * 16; e += kThreads) {
+                    const int t = e >> 4, c = e & 15;
+                    const bool in = t < valid;
+                    const uint4 src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2)[c];
+                    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&src);
+                    float x[8], ss = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        x[j] = __bfloat162float(xb[j]);
+                        ss = fmaf(x[j], x[j], ss);
+                    }
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                    if (in) {
+                        const float r = rsqrtf(ss / kD + p.norm_eps);
+                        const int64_t row = ((tok0 + t) * p.heads_v + h) * kD + 8 * c;
+                        const uint4 zv = *reinterpret_cast<const uint4*>(
+                            static_cast<const __nv_bfloat16*>(p.norm_z) + row);
+                        const __nv_bfloat16* zb = reinterpret_cast<const __nv_bfloat16*>(&zv);
+                        uint4 y;
+                        uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float y0 = x[2 * j] * r * p.norm_w[8 * c + 2 * j] *
+                                             silu_f32(__bfloat162float(zb[2 * j]));
+                            const float y1 = x[2 * j + 1] * r * p.norm_w[8 * c + 2 * j + 1] *
+                                             silu_f32(__bfloat162float(zb[2 * j + 1]));
+                            yw[j] = pack_bf16(y0, y1);
+                        }
+                        *reinterpret_cast<uint4*>(out + row) = y;
+                    }
+                }
             }
         }
         __syncthreads();

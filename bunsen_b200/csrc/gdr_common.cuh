@@ -20,6 +20,18 @@ struct Problem {
     int32_t use_l2norm;
     float l2norm_eps;
     float q_scale;  // 1 / sqrt(d_k)
+    // Steps of the layer fused into the rule (off while the pointers are
+    // null): g and beta from the projections a, b [T, H_v] (gated_delta_net.rs:
+    // 422-426), and the gated RMS norm of the output with z [T, H_v, d_v] in
+    // the output's dtype and its weight [d_v] (:439-440).
+    const void* gate_a = nullptr;
+    const void* gate_b = nullptr;
+    const float* a_log = nullptr;
+    const float* dt_bias = nullptr;
+    int32_t gate_bf16 = 0;
+    const void* norm_z = nullptr;
+    const float* norm_w = nullptr;
+    float norm_eps = 0.f;
 };
 
 // [start, end) of sequence s in the packed token axis. Offsets are clamped
@@ -70,5 +82,25 @@ __device__ __forceinline__ float gate_g(float a, float a_log, float dt_bias) {
     return -expf(a_log) * sp;
 }
 __device__ __forceinline__ float gate_beta(float b) { return 1.f / (1.f + expf(-b)); }
+
+__device__ __forceinline__ float load_gate_input(const void* base, int64_t i, int32_t bf16) {
+    return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
+                : static_cast<const float*>(base)[i];
+}
+
+// g and beta of position-and-head index i = t * H_v + h: from the call's
+// arrays, or produced from the projections when the layer's gates are fused.
+__device__ __forceinline__ void rule_gates(const Problem& p, const float* g, const float* beta,
+                                           int64_t i, int h, float& gi, float& bi) {
+    if (p.gate_a != nullptr) {
+        gi = gate_g(load_gate_input(p.gate_a, i, p.gate_bf16), p.a_log[h], p.dt_bias[h]);
+        bi = gate_beta(load_gate_input(p.gate_b, i, p.gate_bf16));
+    } else {
+        gi = g[i];
+        bi = beta[i];
+    }
+}
+
+__device__ __forceinline__ float silu_f32(float x) { return x / (1.f + __expf(-x)); }
 
 }  // namespace gdr

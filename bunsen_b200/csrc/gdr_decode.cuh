@@ -26,6 +26,7 @@ struct DecodeSmem {
     float red[2][kDecWarps][kDecD];    // per-warp partial k^T S, q^T S
     float delta_s[kDecD];
     float scal[4];                     // |q|^2, |k|^2, -, q.k
+    float nrm[4];                      // per-warp sums of squares of the output
 };
 
 using DecodeState = float[kDecRowsPerWarp][4];
@@ -73,8 +74,9 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
         const int64_t qk_off = (t * p.heads_qk + hq) * kD;
         qk_raw[tid >> 7][tid & 127] = to_f32(((tid < 128) ? q : k)[qk_off + (tid & 127)]);
         const int64_t gate = t * p.heads_v + h;
-        const float decay = __expf(g[gate]);
-        const float bt = beta[gate];
+        float gt, bt;
+        rule_gates(p, g, beta, gate, h, gt, bt);
+        const float decay = __expf(gt);
         __syncthreads();
         if (warp < 3) {  // |q|^2, |k|^2, q.k
             float a[4], b[4];
@@ -108,6 +110,8 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
             red[1][warp][col + c] = pq[c];
         }
         __syncthreads();
+        float o = 0.f;
+        const int64_t orow = (t * p.heads_v + h) * kD;
         if (tid < kD) {
             float read = 0.f, qs = 0.f;
 #pragma unroll
@@ -115,13 +119,25 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
                 read += red[0][w][tid];
                 qs += red[1][w][tid];
             }
-            const float vj = to_f32(v[(t * p.heads_v + h) * kD + tid]);
+            const float vj = to_f32(v[orow + tid]);
             const float d = (vj - read) * bt;
             delta_s[tid] = d;
             const float qk_dot = scal[3] * fq * fk;
-            out[(t * p.heads_v + h) * kD + tid] = from_f32<T>(fmaf(d, qk_dot, qs));
+            o = fmaf(d, qk_dot, qs);
+            if (p.norm_z == nullptr) {
+                out[orow + tid] = from_f32<T>(o);
+            } else {  // the norm reads the output in its own dtype
+                o = to_f32(from_f32<T>(o));
+                const float ss = warp_sum(o * o);
+                if (lane == 0) sh.nrm[warp] = ss;
+            }
         }
         __syncthreads();
+        if (p.norm_z != nullptr && tid < kD) {  // gated RMS norm of the 128 outputs
+            const float r = rsqrtf((sh.nrm[0] + sh.nrm[1] + sh.nrm[2] + sh.nrm[3]) / kD + p.norm_eps);
+            const float z = to_f32(static_cast<const T*>(p.norm_z)[orow + tid]);
+            out[orow + tid] = from_f32<T>(o * r * p.norm_w[tid] * silu_f32(z));
+        }
         float dl[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) dl[c] = delta_s[col + c];

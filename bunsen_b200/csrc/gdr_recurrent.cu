@@ -76,7 +76,9 @@ recurrent_generic(Problem p, const T* __restrict__ q, const T* __restrict__ k,
         __syncthreads();
         const float fq = l2_factor(p, norms[0]) * p.q_scale, fk = l2_factor(p, norms[1]);
         const int64_t gate = t * p.heads_v + h;
-        const float decay = __expf(g[gate]), bt = beta[gate];
+        float gt, bt;
+        rule_gates(p, g, beta, gate, h, gt, bt);
+        const float decay = __expf(gt);
         for (int j = tid; j < dv; j += blockDim.x) {
             float read = 0.f;
             for (int i = 0; i < dk; ++i) {

@@ -130,3 +130,47 @@ def test_reorder_and_bad_source():
     torch.cuda.synchronize()
     assert _lib.load().gdr_device_error() == _lib.GDR_ERR_INVALID
     assert torch.count_nonzero(out[1]) == 0 and torch.equal(out[2], pool[1])
+
+
+def test_gates_and_norm_on_the_split_path():
+    """The split form with fused gates and norm: every segment kind (first,
+    B and M runs, middle and last) stages the projections and normalises."""
+    lens = [700, 64 * 5 + 3, 1, 1500]
+    x = _rand_bf16(lens, state=True, seed=41)
+    gen = torch.Generator(device=DEV).manual_seed(42)
+    t = sum(lens)
+    a = torch.randn(t, 4, device=DEV, generator=gen).bfloat16()
+    b = torch.randn(t, 4, device=DEV, generator=gen).bfloat16()
+    a_log = torch.log(torch.rand(4, device=DEV, generator=gen) * 0.2 + 0.01)
+    dt_bias = torch.randn(4, device=DEV, generator=gen) * 0.1
+    z = torch.randn(t, 4, 128, device=DEV, generator=gen).bfloat16()
+    w = torch.rand(128, device=DEV, generator=gen) + 0.5
+    out, st = GatedDeltaRule(algo="tensor_split", split_chunks=2).chunked(
+        x["q"], x["k"], x["v"], None, None, x["state"], cu_seqlens=x["cu_seqlens"],
+        gates=(a, b, a_log, dt_bias), norm=(z, w, 1e-6))
+    _ok()
+    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias))
+    core, want_st = _oracle("chunked", dict(x, g=torch.from_numpy(g), beta=torch.from_numpy(beta)))
+    want = olayer.gated_norm(_np(torch.from_numpy(core).bfloat16()), _np(z), _np(w), 1e-6)
+    assert rel_err(_np(out), want) < TOL_BF16_OUT
+    assert rel_err(_np(st), want_st) < TOL_BF16_STATE
+
+
+@pytest.mark.parametrize("name", ["toy", "toy_untied"])
+def test_layer0_one_position_at_a_time(golden, name):
+    """The toy layer 0 as a decode: recurrent (gates fused into the generic
+    recurrent kernel, the norm after it) reproduces transformers' output."""
+    d = golden[f"{name}_layer0"]
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    hk = int(d["n_key_heads"])
+    hv, dk, dv = d["v"].shape[2], d["q"].shape[3], d["v"].shape[3]
+    (q, k, v), _ = causal_conv1d(T(d["conv_x"])[None], T(d["conv_w"]), silu=True,
+                                 splits=(hk * dk, 2 * hk * dk))
+    q, k, v = q.reshape(1, -1, hk, dk), k.reshape(1, -1, hk, dk), v.reshape(1, -1, hv, dv)
+    z = T(d["norm_z"]).reshape(1, -1, hv, dv)
+    out, _ = GatedDeltaRule().recurrent(
+        q, k, v, None, None, None,
+        gates=(T(d["a"])[None], T(d["b"])[None], T(d["a_log"]), T(d["dt_bias"])),
+        norm=(z, T(d["norm_w"]), float(d["norm_eps"])))
+    _ok()
+    assert rel_err(_np(out).reshape(-1, dv), d["norm_out"]) < TOL_F32
