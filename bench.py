@@ -438,6 +438,95 @@ def bench_mixed(args, dist, dev, stream, pk, pk_kind) -> dict:
             "roofline": roofline(flops, nbytes, statistics.mean(per), pk, pk_kind, None)}
 
 
+def bench_layer(args, dist, dev, stream, pk, pk_kind) -> dict:
+    """The layer's steps around the rule on this rank's heads of the ragged
+    pack: the causal conv with silu and the q/k/v split (4 taps, f32 states,
+    HBM-bound), the prefill with the gates and gated norm fused, against the
+    plain prefill, and the decode pool's row reorder (HBM-bound)."""
+    from bunsen_b200.layer import causal_conv1d, gated_norm, state_reorder
+
+    w = workloads.get("ragged_prefill")
+    sh = shard_of(w, dist)
+    hq, hv = sh.qk.stop - sh.qk.start, sh.v.stop - sh.v.start
+    gen = torch.Generator(device=dev).manual_seed(61)
+    t, n = w.tokens, w.n_seqs
+    cu = torch.tensor([0] + list(np.cumsum(w.seqlens)), dtype=torch.int32, device=dev)
+    res = {}
+
+    # Conv: x [T, C] bf16, C = 2 H_qk d_k + H_v d_v channels of this rank.
+    c, taps = 2 * hq * w.d_k + hv * w.d_v, 4
+    x = torch.randn(t, c, device=dev, generator=gen).bfloat16()
+    wt = (torch.randn(c, taps, device=dev, generator=gen) * 0.5).bfloat16()
+    st = torch.randn(n, taps - 1, c, device=dev, generator=gen).bfloat16().float()
+    st_out = torch.empty_like(st)
+    splits = (hq * w.d_k, 2 * hq * w.d_k)
+
+    def conv_step():
+        causal_conv1d(x, wt, st, cu_seqlens=cu, silu=True, splits=splits, state_out=st_out)
+
+    total, per = timed(conv_step, args.steps, args.warmup, dist, stream)
+    nbytes = 2 * t * c * 2 + 2 * st.numel() * 4 + wt.numel() * 2
+    ms = total / args.steps
+    res["conv"] = {"value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+                   "channels": c, "taps": taps, "bytes_per_step": nbytes,
+                   "roofline": roofline(0.0, nbytes, statistics.mean(per), pk, pk_kind, None)}
+    del x, st, st_out
+
+    # Prefill with the layer's gates and gated norm fused, against the plain one.
+    full = workloads.make_inputs(w, dev, seed=1234)
+    xin = sh.take(full)
+    del full
+    a = torch.randn(t, hv, device=dev, generator=gen).bfloat16()
+    b = torch.randn(t, hv, device=dev, generator=gen).bfloat16()
+    a_log = torch.log(torch.rand(hv, device=dev, generator=gen) * 0.2 + 0.01)
+    dt_bias = torch.randn(hv, device=dev, generator=gen) * 0.1
+    z = torch.randn(t, hv, w.d_v, device=dev, generator=gen).bfloat16()
+    nw = torch.rand(w.d_v, device=dev, generator=gen) + 0.5
+    rule = GatedDeltaRule(chunk_size=w.chunk)
+    out = torch.empty(t, hv, w.d_v, dtype=torch.bfloat16, device=dev)
+    so = torch.empty(n, hv, w.d_k, w.d_v, dtype=torch.float32, device=dev)
+
+    def fused_step():
+        rule.chunked(xin["q"], xin["k"], xin["v"], None, None, xin["state"], cu_seqlens=cu,
+                     out=out, state_out=so, gates=(a, b, a_log, dt_bias), norm=(z, nw, 1e-6))
+
+    def plain_step():
+        rule.chunked(xin["q"], xin["k"], xin["v"], xin["g"], xin["beta"], xin["state"],
+                     cu_seqlens=cu, out=out, state_out=so)
+
+    def gates_then_norm_step():
+        rule.chunked(xin["q"], xin["k"], xin["v"], None, None, xin["state"], cu_seqlens=cu,
+                     out=out, state_out=so, gates=(a, b, a_log, dt_bias))
+        gated_norm(out, z, nw, 1e-6, out=out)
+
+    tf, _ = timed(fused_step, args.steps, args.warmup, dist, stream)
+    ts, _ = timed(gates_then_norm_step, args.steps, args.warmup, dist, stream)
+    tp, _ = timed(plain_step, args.steps, args.warmup, dist, stream)
+    res["prefill_gates_norm"] = {"value": t / (tf / args.steps * 1e-3), "unit": "tokens/s",
+                                 "ms_per_step": tf / args.steps,
+                                 "separate_norm_ms_per_step": ts / args.steps,
+                                 "plain_ms_per_step": tp / args.steps}
+    del xin, a, b, z, out, so
+
+    # Reorder of the decode workload's state pool (rows permuted).
+    wd = workloads.get("decode")
+    pool = torch.randn(wd.n_seqs, hv, w.d_k, w.d_v, device=dev, generator=gen)
+    dst = torch.empty_like(pool)
+    src = torch.randperm(wd.n_seqs, generator=gen, device=dev).to(torch.int32)
+
+    def reorder_step():
+        state_reorder(pool, src, out=dst)
+
+    total, per = timed(reorder_step, args.steps, args.warmup, dist, stream)
+    nbytes = 2 * pool.numel() * 4
+    ms = total / args.steps
+    res["reorder"] = {"value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+                      "rows": wd.n_seqs, "bytes_per_step": nbytes,
+                      "roofline": roofline(0.0, nbytes, statistics.mean(per), pk, pk_kind, None)}
+    res["gpu_launches"] = {"conv": 2 * args.steps, "reorder": args.steps}
+    return res
+
+
 def run_native(args, dist: Dist) -> None:
     torch.cuda.set_device(dist.local)
     dev = torch.device("cuda", dist.local)
@@ -450,6 +539,7 @@ def run_native(args, dist: Dist) -> None:
     dense = bench_prefill("dense_prefill", args, dist, dev, stream, pk, pk_kind)
     decode = bench_decode(args, dist, dev, stream, pk, pk_kind)
     mixed = bench_mixed(args, dist, dev, stream, pk, pk_kind)
+    layer = bench_layer(args, dist, dev, stream, pk, pk_kind)
     if lib.gdr_device_error() != _lib.GDR_OK:
         raise RuntimeError("a kernel recorded a device-side failure")
     cpu = None
@@ -470,7 +560,7 @@ def run_native(args, dist: Dist) -> None:
                 "gpu_launches": rag["gpu_launches"], "clocks": rag["clocks"],
                 "dense": {k: dense[k] for k in ("value", "unit", "ms_per_step", "roofline",
                                                 "clocks")},
-                "decode": decode, "mixed": mixed}
+                "decode": decode, "mixed": mixed, "layer": layer}
         if "verified" in rag:
             line["verified"] = rag["verified"]
         print(json.dumps(line), flush=True)

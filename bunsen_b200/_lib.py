@@ -77,6 +77,8 @@ SIGNATURES = {
     "gdr_causal_conv1d": (_i32, [ctypes.POINTER(GdrConvParams), _vp, _vp, _vp, _vp, _vp, _vp,
                                  _vp, _vp, _vp]),
     "gdr_state_reorder": (_i32, [_vp, _vp, _vp, _i32, _i32, _sz, _vp]),
+    "gdr_gated_norm": (_i32, [ctypes.c_int64, _i32, _vp, _vp, _vp, ctypes.c_double, _i32, _vp,
+                              _vp]),
     "gdr_mixed_workspace_size": (_sz, [ctypes.POINTER(GdrParams)]),
     "gdr_mixed": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                          _vp, _vp, _vp, _sz, _vp]),

@@ -369,6 +369,18 @@ gdr_status gdr_causal_conv1d(const gdr_conv_params* params, const void* x, const
         weight, state_in, out0, out1, out2, state_out, static_cast<cudaStream_t>(stream)));
 }
 
+gdr_status gdr_gated_norm(int64_t rows, int32_t width, const void* x, const void* z,
+                          const float* weight, double eps, int32_t dtype, void* out,
+                          void* stream) {
+    if (rows < 0 || width <= 0 || !(eps >= 0.0)) return GDR_ERR_INVALID;
+    if (dtype != GDR_DTYPE_F32 && dtype != GDR_DTYPE_BF16) return GDR_ERR_INVALID;
+    if (rows == 0) return GDR_OK;
+    if (x == nullptr || z == nullptr || weight == nullptr || out == nullptr) return GDR_ERR_INVALID;
+    return from_cuda(gdr::launch_gated_norm(dtype, rows, width, x, z, weight,
+                                            static_cast<float>(eps), out,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
 gdr_status gdr_state_reorder(const void* src, void* dst, const int32_t* sources, int32_t rows,
                              int32_t src_rows, size_t row_bytes, void* stream) {
     if (rows < 0 || src_rows < 0 || row_bytes % 4 != 0) return GDR_ERR_INVALID;

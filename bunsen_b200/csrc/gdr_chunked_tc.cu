@@ -78,6 +78,9 @@ constexpr uint32_t kTileBytes = 8192;     // one 64 x 64 bf16 TMA box
 constexpr uint32_t kSmemBytes = kOffMisc + 3072 + 1024;  // + alignment slack
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kOsStride = 160;  // bf16 row stride of the output staging tile
+constexpr uint32_t kOffZ = 20480;  // in ST: a chunk's z rows [64][128] bf16 (gated norm)
+static_assert(kC * kOsStride * 2 <= kOffZ && kOffZ + kC * kD * 2 <= kOffMisc - kOffST,
+              "the z rows sit between the output staging and the end of ST");
 
 struct Misc {
     float gam[kC];  // cumulative log decay within the chunk
@@ -92,7 +95,6 @@ struct Misc {
     float gstage[2][kC];  // the next chunk's g and beta, landing by cp.async
     uint64_t bar_tma, bar_mma, bar_qs;  // tiles landed; MMA groups; the (Q S)^T group
     uint32_t tmem_base;
-    int failed;
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -314,7 +316,6 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         mbar_init(&ms.bar_tma, 1);
         mbar_init(&ms.bar_mma, 1);
         mbar_init(&ms.bar_qs, 1);
-        ms.failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
@@ -385,32 +386,27 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     auto gates_landed = [] { asm volatile("cp.async.wait_group 0;" ::: "memory"); };
-    // Warp 0: chunk ci's staged gates into the chunk's arrays, the log decay
-    // as its running sum (positions 2 lane, 2 lane + 1). Fused gates: g and
-    // beta from the staged projections, zero past the end (as the zero-filled
-    // g and beta are).
-    auto put_gates = [&](int ci) {
-        float pg0 = ms.gstage[0][2 * lane], pg1 = ms.gstage[0][2 * lane + 1];
-        float pb0 = ms.gstage[1][2 * lane], pb1 = ms.gstage[1][2 * lane + 1];
-        if (p.gate_a != nullptr) {
-            const float al = p.a_log[h], db = p.dt_bias[h];
-            float* pg[2] = {&pg0, &pg1};
-            float* pb[2] = {&pb0, &pb1};
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int64_t pos = static_cast<int64_t>(ci) * kC + 2 * lane + u;
-                const bool in = pos < len;
-                float a = *pg[u], b = *pb[u];
-                if (p.gate_bf16) {
-                    const int64_t i = (t0 + (in ? pos : len - 1)) * p.heads_v + h;
-                    const int sh = (i & 1) ? 16 : 0;
-                    a = __uint_as_float((__float_as_uint(a) >> sh) << 16);
-                    b = __uint_as_float((__float_as_uint(b) >> sh) << 16);
-                }
-                *pg[u] = in ? gate_g(a, al, db) : 0.f;
-                *pb[u] = in ? gate_beta(b) : 0.f;
-            }
+    // Threads 0..127, after their own copy landed: with the layer's gates
+    // fused, chunk ci's staged projection word becomes g (tid < 64) or beta,
+    // zero past the end (as the zero-filled g and beta are).
+    auto convert_gates = [&](int ci) {
+        if (p.gate_a == nullptr) return;
+        const int t = tid & (kC - 1), which = tid >> 6;
+        const int64_t pos = static_cast<int64_t>(ci) * kC + t;
+        float x = ms.gstage[which][t];
+        if (p.gate_bf16) {
+            const int64_t i = (t0 + (pos < len ? pos : len - 1)) * p.heads_v + h;
+            x = __uint_as_float((__float_as_uint(x) >> ((i & 1) ? 16 : 0)) << 16);
         }
+        ms.gstage[which][t] = pos >= len ? 0.f
+                              : which   ? gate_beta(x)
+                                        : gate_g(x, p.a_log[h], p.dt_bias[h]);
+    };
+    // Warp 0: the staged gates into the chunk's arrays, the log decay as its
+    // running sum (positions 2 lane, 2 lane + 1).
+    auto put_gates = [&] {
+        const float pg0 = ms.gstage[0][2 * lane], pg1 = ms.gstage[0][2 * lane + 1];
+        const float pb0 = ms.gstage[1][2 * lane], pb1 = ms.gstage[1][2 * lane + 1];
         float incl = pg0 + pg1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -431,9 +427,10 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     if (tid < 2 * kC && n_chunks > 0) {
         stage_gates(0);
         gates_landed();
+        convert_gates(0);
     }
     __syncthreads();
-    if (warp == 0 && n_chunks > 0) put_gates(0);
+    if (warp == 0 && n_chunks > 0) put_gates();
 
     // The initial state, transposed into TMEM: lane d holds S[:, d].
     {
@@ -465,17 +462,19 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         }
         umma_commit(&ms.bar_mma);
     };
-    bool ok = true;
+    // A wait that runs out marks this thread; the CTA learns of it at the
+    // next __syncthreads_or, so every thread leaves the loop together.
+    int fail = 0;
     auto wait = [&](uint64_t* bar, uint32_t& ph) {
         if (!mbar_wait(bar, ph, kWaitLimitNs)) {
-            ms.failed = 1;
+            fail = 1;
             atomicOr(&g_tc_error, 1);
         }
         ph ^= 1u;
     };
 
 #pragma unroll 1
-    for (int ci = 0; ci < n_chunks && ok; ++ci) {
+    for (int ci = 0; ci < n_chunks; ++ci) {
         const int64_t tok0 = t0 + static_cast<int64_t>(ci) * kC;
         const int64_t left = len - static_cast<int64_t>(ci) * kC;
         const int valid = static_cast<int>(left < kC ? left : kC);
@@ -510,7 +509,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             ms.glf[row] = ms.gl[row] - lg2(fk);
         }
         tc_fence_before();
-        __syncthreads();
+        // Every thread is past the previous chunk's output (its staging reads
+        // end before (f) writes ST), and a failure anywhere ends the loop.
+        if (__syncthreads_or(fail)) break;
         // (f) Per-position factors; rows of L (f32) and of intra (bf16 operand).
         const float decay = __expf(ms.gam[kC - 1]);
         if (tid < kC) {
@@ -658,7 +659,10 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             }
             store_half_row_sw128(AB, row, 4 * hf, vn);
         }
-        if (tid < 2 * kC) gates_landed();
+        if (tid < 2 * kC) {
+            gates_landed();
+            if (ci + 1 < n_chunks) convert_gates(ci + 1);
+        }
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
@@ -678,12 +682,30 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             umma_commit(&ms.bar_mma);
         }
         // (p) The next chunk's gates (this chunk's are no longer read).
-        if (warp == 0 && ci + 1 < n_chunks) put_gates(ci + 1);
+        if (warp == 0 && ci + 1 < n_chunks) put_gates();
         wait(&ms.bar_mma, ph_mma);
         wait(&ms.bar_qs, ph_qs);  // done with the G4/G5 group before it
         tc_fence_after();
         // (r) The next chunk's tiles load while this chunk's output is written.
+        //     With the gated norm, this chunk's z rows land in the tail of ST
+        //     (free once the Q S group is done), each thread copying the row
+        //     pieces it normalises in (s).
         if (tid == 0 && ci + 1 < n_chunks) issue_tiles(ci + 1);
+        if (with_out && p.norm_z != nullptr) {
+            const int c = tid & 15;
+#pragma unroll
+            for (int u = 0; u < kC / 16; ++u) {
+                const int t = (tid >> 4) + 16 * u;
+                const int tt = t < valid ? t : 0;
+                const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.norm_z) +
+                                           ((tok0 + tt) * p.heads_v + h) * kD + 8 * c;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                                 smem_u32(ST + kOffZ + t * 256 + 16 * c)),
+                             "l"(src), "r"(t < valid ? 16 : 0)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
         // (s) O^T = (Q S)^T diag(cq) + (intra V_new)^T -> bf16 staging [t][d].
         if constexpr (with_out) {
             float qs[32], iv[32];
@@ -738,7 +760,13 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 }
             } else {
                 // The layer's gated RMS norm of each output row: 16 lanes hold
-                // a row's 128 features (8 each) and reduce over them.
+                // a row's 128 features (8 each) and reduce over them; z from
+                // the rows staged at (r).
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+                const int cw = tid & 15;
+                const float4 w0 = reinterpret_cast<const float4*>(p.norm_w)[2 * cw];
+                const float4 w1 = reinterpret_cast<const float4*>(p.norm_w)[2 * cw + 1];
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll 1
                 for (int e = tid; e < kC * 16; e += kThreads) {
                     const int t = e >> 4, c = e & 15;
@@ -756,16 +784,15 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                     if (in) {
                         const float r = rsqrtf(ss / kD + p.norm_eps);
                         const int64_t row = ((tok0 + t) * p.heads_v + h) * kD + 8 * c;
-                        const uint4 zv = *reinterpret_cast<const uint4*>(
-                            static_cast<const __nv_bfloat16*>(p.norm_z) + row);
+                        const uint4 zv = *reinterpret_cast<const uint4*>(ST + kOffZ + t * 256 + 16 * c);
                         const __nv_bfloat16* zb = reinterpret_cast<const __nv_bfloat16*>(&zv);
                         uint4 y;
                         uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            const float y0 = x[2 * j] * r * p.norm_w[8 * c + 2 * j] *
-                                             silu_f32(__bfloat162float(zb[2 * j]));
-                            const float y1 = x[2 * j + 1] * r * p.norm_w[8 * c + 2 * j + 1] *
+                            const float y0 =
+                                x[2 * j] * r * wv[2 * j] * silu_f32(__bfloat162float(zb[2 * j]));
+                            const float y1 = x[2 * j + 1] * r * wv[2 * j + 1] *
                                              silu_f32(__bfloat162float(zb[2 * j + 1]));
                             yw[j] = pack_bf16(y0, y1);
                         }
@@ -774,9 +801,8 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 }
             }
         }
-        __syncthreads();
-        ok = ms.failed == 0;
     }
+    const bool ok = !__syncthreads_or(fail);
 
     // The final state, S^T lane d -> S[:, d].
     if (ok) {

@@ -101,6 +101,7 @@ __device__ __forceinline__ void rule_gates(const Problem& p, const float* g, con
     }
 }
 
-__device__ __forceinline__ float silu_f32(float x) { return x / (1.f + __expf(-x)); }
+// x sigmoid(x) with the fast exponential and divide (0 for very negative x).
+__device__ __forceinline__ float silu_f32(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 }  // namespace gdr

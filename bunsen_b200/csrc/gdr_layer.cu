@@ -24,7 +24,7 @@ cudaError_t take_layer_error(int* flag) {
 
 namespace {
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 // ---- causal depthwise convolution (causal_conv.rs:36-69) -------------------
 struct Conv {
@@ -127,6 +127,110 @@ conv_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ weight,
     }
 }
 
+// Two adjacent channels per thread (4- or 8-byte accesses, a warp's row
+// access one 128- or 256-byte line): few registers, so a full SM of warps
+// keeps loads in flight while others compute; the positions of a window
+// taken eight at a time, all eight rows loaded before any is used. Needs an
+// even C, even splits and 8-byte-aligned buffers.
+template <typename T>
+__device__ __forceinline__ float2 load2(const T* p);
+template <>
+__device__ __forceinline__ float2 load2<float>(const float* p) {
+    return *reinterpret_cast<const float2*>(p);
+}
+template <>
+__device__ __forceinline__ float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+template <typename T>
+__device__ __forceinline__ void store2(T* p, float a, float b);
+template <>
+__device__ __forceinline__ void store2<float>(float* p, float a, float b) {
+    *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+template <>
+__device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* p, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kConvThreads)
+conv_vec_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ weight,
+                const float* state, T* out0, T* out1, T* out2) {
+    constexpr int kRows = 8;
+    const int C = p.channels;
+    const int c0 = (blockIdx.x * kConvThreads + threadIdx.x) * 2;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kConvTokens;
+    if (c0 >= C || t0 >= p.tokens) return;
+    float w0[K], w1[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        w0[j] = to_f32(weight[static_cast<int64_t>(c0) * K + j]);
+        w1[j] = to_f32(weight[static_cast<int64_t>(c0 + 1) * K + j]);
+    }
+    auto from_state = [&](int s, int i) {
+        return *reinterpret_cast<const float2*>(state + (static_cast<int64_t>(s) * (K - 1) + i) * C + c0);
+    };
+    int s = conv_seq_of(p, t0);
+    int64_t start, end;
+    conv_span(p, s, start, end);
+    float2 h[K - 1];
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+        const int64_t u = t0 - (K - 1) + i;
+        h[i] = u >= start ? load2(x + u * C + c0)
+               : (state && start - u <= K - 1) ? from_state(s, static_cast<int>((K - 1) - (start - u)))
+                                               : make_float2(0.f, 0.f);
+    }
+    T* out;
+    int64_t stride;
+    int col;
+    if (c0 < p.split0) {
+        out = out0, stride = p.split0, col = c0;
+    } else if (c0 < p.split1) {
+        out = out1, stride = p.split1 - p.split0, col = c0 - p.split0;
+    } else {
+        out = out2, stride = C - p.split1, col = c0 - p.split1;
+    }
+    const int64_t t1 = t0 + kConvTokens < p.tokens ? t0 + kConvTokens : p.tokens;
+#pragma unroll 1
+    for (int64_t tb = t0; tb < t1; tb += kRows) {
+        float2 xr[kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+            xr[r] = tb + r < t1 ? load2(x + (tb + r) * C + c0) : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int64_t t = tb + r;
+            if (t < t1) {
+                while (t >= end && s + 1 < p.n_seqs) {  // into the next sequence
+                    ++s;
+                    conv_span(p, s, start, end);
+#pragma unroll
+                    for (int i = 0; i < K - 1; ++i)
+                        h[i] = state ? from_state(s, i) : make_float2(0.f, 0.f);
+                }
+                float a0 = h[0].x * w0[0], a1 = h[0].y * w1[0];
+#pragma unroll
+                for (int j = 1; j < K - 1; ++j) {
+                    a0 = fmaf(h[j].x, w0[j], a0);
+                    a1 = fmaf(h[j].y, w1[j], a1);
+                }
+                a0 = fmaf(xr[r].x, w0[K - 1], a0);
+                a1 = fmaf(xr[r].y, w1[K - 1], a1);
+                if (p.silu) {
+                    a0 = silu_f(a0);
+                    a1 = silu_f(a1);
+                }
+                store2(out + t * stride + col, a0, a1);
+#pragma unroll
+                for (int i = 0; i + 1 < K - 1; ++i) h[i] = h[i + 1];
+                h[K - 2] = xr[r];
+            }
+        }
+    }
+}
+
 // The next state, per (sequence, channel): the last K - 1 inputs of the
 // window [state, x], read in full before it is written (the state may be
 // updated in place).
@@ -194,6 +298,43 @@ __global__ void gated_norm_kernel(int64_t rows, int width, const T* x, const T* 
     }
 }
 
+// The bf16, 128-feature rows of the rule's output: a warp takes kNormRows
+// rows, each lane 4 features (8-byte accesses) of each, every load of the
+// rows issued before any is used.
+constexpr int kNormRows = 4;
+__global__ void __launch_bounds__(256)
+gated_norm_bf16_128(int64_t rows, const __nv_bfloat16* x, const __nv_bfloat16* __restrict__ z,
+                    const float* __restrict__ weight, float eps, __nv_bfloat16* out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r0 = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * kNormRows;
+    if (r0 >= rows) return;
+    const float4 wv = reinterpret_cast<const float4*>(weight)[lane];
+    uint2 xv[kNormRows], zv[kNormRows];
+#pragma unroll
+    for (int r = 0; r < kNormRows; ++r) {
+        const int64_t row = r0 + r < rows ? r0 + r : r0;
+        xv[r] = reinterpret_cast<const uint2*>(x + row * 128)[lane];
+        zv[r] = reinterpret_cast<const uint2*>(z + row * 128)[lane];
+    }
+#pragma unroll
+    for (int r = 0; r < kNormRows; ++r) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xv[r].x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xv[r].y));
+        const float2 za = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zv[r].x));
+        const float2 zb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&zv[r].y));
+        const float ss = warp_sum(a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y);
+        const float rs = rsqrtf(ss / 128.f + eps);
+        if (r0 + r < rows) {
+            uint2 y;
+            *reinterpret_cast<__nv_bfloat162*>(&y.x) = __floats2bfloat162_rn(
+                a.x * rs * wv.x * silu_f(za.x), a.y * rs * wv.y * silu_f(za.y));
+            *reinterpret_cast<__nv_bfloat162*>(&y.y) = __floats2bfloat162_rn(
+                b.x * rs * wv.z * silu_f(zb.x), b.y * rs * wv.w * silu_f(zb.y));
+            reinterpret_cast<uint2*>(out + (r0 + r) * 128)[lane] = y;
+        }
+    }
+}
+
 // ---- state reorder (state.rs:112-135) --------------------------------------
 // dst row r <- src row sources[r]; `words` 16-byte (or 4-byte) words per row.
 template <typename W>
@@ -221,8 +362,20 @@ int grid_for(int64_t n, int block) {
 template <typename T, int K>
 void launch_conv_k(const Conv& p, const void* x, const void* w, const float* st, void* o0,
                    void* o1, void* o2, cudaStream_t s) {
-    const dim3 grid((p.channels + kConvThreads - 1) / kConvThreads,
-                    static_cast<unsigned>((p.tokens + kConvTokens - 1) / kConvTokens));
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(st) |
+                         reinterpret_cast<uintptr_t>(o0) | reinterpret_cast<uintptr_t>(o1) |
+                         reinterpret_cast<uintptr_t>(o2);
+    const bool vec = p.channels % 2 == 0 && p.split0 % 2 == 0 && p.split1 % 2 == 0 &&
+                     (al & 7) == 0;
+    const unsigned ty = static_cast<unsigned>((p.tokens + kConvTokens - 1) / kConvTokens);
+    if (vec) {
+        const dim3 grid((p.channels / 2 + kConvThreads - 1) / kConvThreads, ty);
+        conv_vec_kernel<T, K><<<grid, kConvThreads, 0, s>>>(
+            p, static_cast<const T*>(x), static_cast<const T*>(w), st, static_cast<T*>(o0),
+            static_cast<T*>(o1), static_cast<T*>(o2));
+        return;
+    }
+    const dim3 grid((p.channels + kConvThreads - 1) / kConvThreads, ty);
     conv_kernel<T, K><<<grid, kConvThreads, 0, s>>>(
         p, static_cast<const T*>(x), static_cast<const T*>(w), st, static_cast<T*>(o0),
         static_cast<T*>(o1), static_cast<T*>(o2));
@@ -287,6 +440,15 @@ cudaError_t launch_gates(int dtype, int64_t n, int heads, const void* a, const v
 cudaError_t launch_gated_norm(int dtype, int64_t rows, int width, const void* x, const void* z,
                               const float* weight, float eps, void* out, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) |
+                         reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(weight);
+    if (dtype == GDR_DTYPE_BF16 && width == 128 && (al & 15) == 0) {
+        const int64_t warps = (rows + kNormRows - 1) / kNormRows;
+        gated_norm_bf16_128<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(
+            rows, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z),
+            weight, eps, static_cast<__nv_bfloat16*>(out));
+        return cudaGetLastError();
+    }
     const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
     if (dtype == GDR_DTYPE_BF16)
         gated_norm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(

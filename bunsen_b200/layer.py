@@ -5,6 +5,7 @@ libgdr's C ABI (include/gdr.h):
   (``ops/transformers/linear_attention/causal_conv.rs:36-69``), optionally
   with the layer's silu and its q / k / v channel split
   (``blocks/transformers/mixers/gated_delta_net.rs:396-420``);
+* ``gated_norm`` -- ``GatedNorm`` (``gated_delta_net.rs:439-440``) on its own;
 * ``state_reorder`` -- ``DeltaNetState::reorder`` (``state.rs:112-135``).
 
 The gates and the gated norm run with the rule itself:
@@ -65,6 +66,26 @@ def causal_conv1d(x, weight, state=None, *, cu_seqlens=None, silu=False, splits=
         _ptr(state_out) if with_state else None, _ptr(cu_seqlens), _stream(x.device))
     _lib.check("gdr_causal_conv1d", status)
     return (outs[0] if splits is None else tuple(outs)), (state_out if with_state else None)
+
+
+def gated_norm(x, z, weight, eps, out=None):
+    """bunsen's ``GatedNorm`` (``gated_delta_net.rs:439-440``): ``rmsnorm(x) *
+    weight * silu(z)`` over the last axis; x and z share shape and dtype;
+    ``out`` may be ``x``."""
+    if x.device.type != "cuda":
+        raise RuntimeError("libgdr runs on CUDA tensors only")
+    if x.dtype not in _DTYPES or z.dtype != x.dtype or z.shape != x.shape:
+        raise TypeError("x and z share one shape and one dtype, f32 or bf16")
+    x, z = x.contiguous(), z.contiguous()
+    weight = weight.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    width = x.shape[-1]
+    status = _lib.load().gdr_gated_norm(x.numel() // width if width else 0, width, x.data_ptr(),
+                                        z.data_ptr(), weight.data_ptr(), float(eps),
+                                        _DTYPES[x.dtype], out.data_ptr(), _stream(x.device))
+    _lib.check("gdr_gated_norm", status)
+    return out
 
 
 def state_reorder(src, sources, out=None):

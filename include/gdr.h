@@ -198,6 +198,13 @@ gdr_status gdr_recurrent_layer(const gdr_params* params, const void* q, const vo
                                const gdr_layer_io* io, const float* state_in, void* out,
                                float* state_out, const int32_t* cu_seqlens, void* stream);
 
+/* The layer's gated RMS norm on its own (gated_delta_net.rs:439-440, GatedNorm):
+ * out = rmsnorm(x) * weight * silu(z) over each row of `width` features; x, z
+ * and out [rows, width] in `dtype`, weight [width] f32; out may be x. */
+gdr_status gdr_gated_norm(int64_t rows, int32_t width, const void* x, const void* z,
+                          const float* weight, double eps, int32_t dtype, void* out,
+                          void* stream);
+
 /* DeltaNetState::reorder (state.rs:112-135) on device: row r of dst becomes row
  * sources[r] of src, for `rows` rows of row_bytes bytes (a multiple of 4);
  * sources is device memory; src and dst must not overlap. A source outside

@@ -30,11 +30,11 @@ def _ok():
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("taps", [2, 4, 7])
 @pytest.mark.parametrize("with_state", [False, True])
-def test_conv_packed_against_oracle(dtype, taps, with_state):
+@pytest.mark.parametrize("c", [200, 203])  # 16-byte vectors / one channel per thread
+def test_conv_packed_against_oracle(dtype, taps, with_state, c):
     gen = torch.Generator(device=DEV).manual_seed(taps)
     lens = [300, 1, 0, 2, 131, 64, 3]
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=DEV)
-    c = 200
     x = torch.randn(sum(lens), c, device=DEV, generator=gen).to(dtype)
     w = (torch.randn(c, taps, device=DEV, generator=gen) * 0.5).to(dtype)
     s0 = (torch.randn(len(lens), taps - 1, c, device=DEV, generator=gen).to(dtype).float()
