@@ -6,6 +6,7 @@
 // them are HBM-bound elementwise or row work on the CUDA cores: coalesced
 // loads along the channel axis, f32 arithmetic, one pass over the data.
 #include <cmath>
+#include <type_traits>
 
 #include "gdr_common.cuh"
 
@@ -231,6 +232,130 @@ conv_vec_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ wei
     }
 }
 
+// bf16 with C a multiple of 8: a CTA walks kStageSpan positions of 256
+// channels (two per thread), the rows of each 16-position window staged into
+// shared memory by cp.async while the window before is computed, so the
+// loads stay in flight whatever the threads are doing (16 KiB per CTA; the
+// registers, not the staging, bound the CTAs per SM). On B200, 131 072
+// positions x 8192 channels run at 0.66 of the measured HBM copy rate, 0.47
+// with the register-only kernel.
+constexpr int kStageRows = 16, kStageCols = 256, kStageSpan = 512;
+constexpr uint32_t kStageBytes = 2u * kStageRows * kStageCols * 2;  // two windows
+
+template <int K>
+__global__ void __launch_bounds__(kConvThreads)
+conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
+                   const __nv_bfloat16* __restrict__ weight, const float* state,
+                   __nv_bfloat16* out0, __nv_bfloat16* out1, __nv_bfloat16* out2) {
+    extern __shared__ __align__(16) uint8_t conv_smem[];
+    auto* buf = reinterpret_cast<__nv_bfloat16*>(conv_smem);  // [2][64][256]
+    const int C = p.channels, tid = threadIdx.x;
+    const int cb = blockIdx.x * kStageCols;
+    const int c0 = cb + 2 * tid;
+    const int64_t T0 = static_cast<int64_t>(blockIdx.y) * kStageSpan;
+    if (T0 >= p.tokens) return;
+    const int64_t T1 = T0 + kStageSpan < p.tokens ? T0 + kStageSpan : p.tokens;
+    const int windows = static_cast<int>((T1 - T0 + kStageRows - 1) / kStageRows);
+    auto load_window = [&](int w) {  // kStageRows rows x 32 16-byte pieces
+        __nv_bfloat16* dst = buf + (w & 1) * kStageRows * kStageCols;
+#pragma unroll 4
+        for (int e = tid; e < kStageRows * (kStageCols / 8); e += kConvThreads) {
+            const int r = e / (kStageCols / 8), piece = e % (kStageCols / 8);
+            const int64_t t = T0 + static_cast<int64_t>(w) * kStageRows + r;
+            const int c = cb + 8 * piece;
+            const bool in = t < T1 && c < C;
+            const __nv_bfloat16* src = x + (in ? t * C + c : 0);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                             static_cast<uint32_t>(__cvta_generic_to_shared(dst + r * kStageCols + 8 * piece))),
+                         "l"(src), "r"(in ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load_window(0);
+    const bool active = c0 < C;
+    float w0[K], w1[K];
+    float2 h[K - 1];
+    int s = 0;
+    int64_t start = 0, end = 0;
+    __nv_bfloat16* out = nullptr;
+    int64_t stride = 0;
+    int col = 0;
+    if (active) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            w0[j] = to_f32(weight[static_cast<int64_t>(c0) * K + j]);
+            w1[j] = to_f32(weight[static_cast<int64_t>(c0 + 1) * K + j]);
+        }
+        s = conv_seq_of(p, T0);
+        conv_span(p, s, start, end);
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) {
+            const int64_t u = T0 - (K - 1) + i;
+            h[i] = u >= start ? load2(x + u * C + c0)
+                   : (state && start - u <= K - 1)
+                       ? *reinterpret_cast<const float2*>(
+                             state + (static_cast<int64_t>(s) * (K - 1) + (K - 1) - (start - u)) * C + c0)
+                       : make_float2(0.f, 0.f);
+        }
+        if (c0 < p.split0) {
+            out = out0, stride = p.split0, col = c0;
+        } else if (c0 < p.split1) {
+            out = out1, stride = p.split1 - p.split0, col = c0 - p.split0;
+        } else {
+            out = out2, stride = C - p.split1, col = c0 - p.split1;
+        }
+    }
+#pragma unroll 1
+    for (int w = 0; w < windows; ++w) {
+        if (w + 1 < windows) {
+            load_window(w + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();  // window w has landed for every thread
+        if (active) {
+            const __nv_bfloat16* rows = buf + (w & 1) * kStageRows * kStageCols + 2 * tid;
+            const int64_t tw = T0 + static_cast<int64_t>(w) * kStageRows;
+            const int n = static_cast<int>(T1 - tw < kStageRows ? T1 - tw : kStageRows);
+#pragma unroll 4
+            for (int r = 0; r < n; ++r) {
+                const int64_t t = tw + r;
+                while (t >= end && s + 1 < p.n_seqs) {  // into the next sequence
+                    ++s;
+                    conv_span(p, s, start, end);
+#pragma unroll
+                    for (int i = 0; i < K - 1; ++i)
+                        h[i] = state ? *reinterpret_cast<const float2*>(
+                                           state + (static_cast<int64_t>(s) * (K - 1) + i) * C + c0)
+                                     : make_float2(0.f, 0.f);
+                }
+                const float2 xt =
+                    __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rows + r * kStageCols));
+                float a0 = h[0].x * w0[0], a1 = h[0].y * w1[0];
+#pragma unroll
+                for (int j = 1; j < K - 1; ++j) {
+                    a0 = fmaf(h[j].x, w0[j], a0);
+                    a1 = fmaf(h[j].y, w1[j], a1);
+                }
+                a0 = fmaf(xt.x, w0[K - 1], a0);
+                a1 = fmaf(xt.y, w1[K - 1], a1);
+                if (p.silu) {
+                    a0 = silu_f(a0);
+                    a1 = silu_f(a1);
+                }
+                *reinterpret_cast<__nv_bfloat162*>(out + t * stride + col) =
+                    __floats2bfloat162_rn(a0, a1);
+#pragma unroll
+                for (int i = 0; i + 1 < K - 1; ++i) h[i] = h[i + 1];
+                h[K - 2] = xt;
+            }
+        }
+        __syncthreads();  // window w's buffer is free for window w + 2
+    }
+}
+
 // The next state, per (sequence, channel): the last K - 1 inputs of the
 // window [state, x], read in full before it is written (the state may be
 // updated in place).
@@ -368,6 +493,19 @@ void launch_conv_k(const Conv& p, const void* x, const void* w, const float* st,
     const bool vec = p.channels % 2 == 0 && p.split0 % 2 == 0 && p.split1 % 2 == 0 &&
                      (al & 7) == 0;
     const unsigned ty = static_cast<unsigned>((p.tokens + kConvTokens - 1) / kConvTokens);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        if (vec && p.channels % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+            cudaFuncSetAttribute(conv_staged_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kStageBytes));
+            const dim3 grid((p.channels + kStageCols - 1) / kStageCols,
+                            static_cast<unsigned>((p.tokens + kStageSpan - 1) / kStageSpan));
+            conv_staged_kernel<K><<<grid, kConvThreads, kStageBytes, s>>>(
+                p, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), st,
+                static_cast<__nv_bfloat16*>(o0), static_cast<__nv_bfloat16*>(o1),
+                static_cast<__nv_bfloat16*>(o2));
+            return;
+        }
+    }
     if (vec) {
         const dim3 grid((p.channels / 2 + kConvThreads - 1) / kConvThreads, ty);
         conv_vec_kernel<T, K><<<grid, kConvThreads, 0, s>>>(
