@@ -142,3 +142,41 @@ def test_host_call_rejects_malformed_offsets_before_any_copy():
         p = _params(n_seqs=3, seq_len=8, batch=0)
         assert lib.gdr_chunked_host(ctypes.byref(p), d, d, d, d, d, None, d, d,
                                     ctypes.cast(arr, ctypes.c_void_p), None) == _lib.GDR_ERR_INVALID
+
+
+def test_layer_entry_points_reject_bad_arguments_before_any_launch():
+    """The layer steps' entry points check shapes and options on the host and
+    answer GDR_ERR_INVALID (or UNSUPPORTED) before touching the device."""
+    lib = _lib.load()
+    d = ctypes.c_void_p(16)
+    conv = lambda **kw: lib.gdr_causal_conv1d(  # noqa: E731
+        ctypes.byref(_lib.GdrConvParams(**dict(dict(batch=1, seq_len=4, channels=8, taps=4,
+                                                     split0=8, split1=8, dtype=0), **kw))),
+        d, d, None, d, d, d, None, None, None)
+    assert conv(taps=1) == _lib.GDR_ERR_INVALID          # causal_conv.rs:47
+    assert conv(taps=9) == _lib.GDR_ERR_UNSUPPORTED
+    assert conv(split0=9, split1=9) == _lib.GDR_ERR_INVALID
+    assert conv(split0=6, split1=4) == _lib.GDR_ERR_INVALID
+    assert conv(dtype=5) == _lib.GDR_ERR_INVALID
+    assert conv(channels=0) == _lib.GDR_ERR_INVALID
+    norm = lib.gdr_gated_norm
+    assert norm(4, 0, d, d, d, 1e-6, 0, d, None) == _lib.GDR_ERR_INVALID
+    assert norm(4, 8, d, d, d, -1.0, 0, d, None) == _lib.GDR_ERR_INVALID
+    assert norm(4, 8, d, d, d, 1e-6, 3, d, None) == _lib.GDR_ERR_INVALID
+    assert norm(0, 8, None, None, None, 1e-6, 0, None, None) == _lib.GDR_OK  # nothing to do
+    buf = (ctypes.c_uint8 * 256)()
+    base = ctypes.cast(buf, ctypes.c_void_p).value
+    reorder = lib.gdr_state_reorder
+    assert reorder(base, base + 32, d, 4, 4, 16, None) == _lib.GDR_ERR_INVALID  # overlap
+    assert reorder(base, base + 128, d, 4, 4, 6, None) == _lib.GDR_ERR_INVALID  # not words
+    assert reorder(base, base + 128, d, 0, 4, 16, None) == _lib.GDR_OK         # no rows
+    p = _params()
+    io = _lib.GdrLayerIO(gate_a=16, gate_b=16, a_log=16, dt_bias=16, gate_dtype=0)
+    assert lib.gdr_chunked_layer(ctypes.byref(p), d, d, d, d, None, ctypes.byref(io), None, d,
+                                 d, None, None) == _lib.GDR_ERR_INVALID  # g given with gates
+    io = _lib.GdrLayerIO(gate_a=16, gate_b=16, a_log=16, dt_bias=16, gate_dtype=7)
+    assert lib.gdr_recurrent_layer(ctypes.byref(p), d, d, d, None, None, ctypes.byref(io), None,
+                                   d, d, None, None) == _lib.GDR_ERR_INVALID
+    io = _lib.GdrLayerIO(norm_z=16, norm_weight=16, norm_eps=-1.0)
+    assert lib.gdr_chunked_layer(ctypes.byref(p), d, d, d, d, d, ctypes.byref(io), None, d, d,
+                                 None, None) == _lib.GDR_ERR_INVALID
