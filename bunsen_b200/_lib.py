@@ -74,6 +74,9 @@ SIGNATURES = {
     "gdr_chunked_host": (_i32, _RULE_ARGS),
     "gdr_chunked_layer": (_i32, _LAYER_ARGS),
     "gdr_recurrent_layer": (_i32, _LAYER_ARGS),
+    "gdr_mixed_layer": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp,
+                               ctypes.POINTER(GdrLayerIO), _vp, _vp, _i32, _vp, _vp, _vp, _sz,
+                               _vp]),
     "gdr_causal_conv1d": (_i32, [ctypes.POINTER(GdrConvParams), _vp, _vp, _vp, _vp, _vp, _vp,
                                  _vp, _vp, _vp]),
     "gdr_state_reorder": (_i32, [_vp, _vp, _vp, _i32, _i32, _sz, _vp]),

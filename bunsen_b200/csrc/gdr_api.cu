@@ -539,6 +539,58 @@ gdr_status gdr_mixed(const gdr_params* params, const void* q, const void* k, con
                                           static_cast<cudaStream_t>(stream)));
 }
 
+gdr_status gdr_mixed_layer(const gdr_params* params, const void* q, const void* k,
+                           const void* v, const float* g, const float* beta,
+                           const gdr_layer_io* io, float* state_pool,
+                           const int32_t* state_slots, int32_t n_slots, void* out,
+                           const int32_t* cu_seqlens, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+    if (io == nullptr || (io->gate_a == nullptr && io->norm_z == nullptr))
+        return gdr_mixed(params, q, k, v, g, beta, state_pool, state_slots, n_slots, out,
+                         cu_seqlens, workspace, workspace_bytes, stream);
+    if (cu_seqlens == nullptr) return GDR_ERR_INVALID;
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p);
+    if (st != GDR_OK) return st;
+    if (params->chunk_size <= 0) return GDR_ERR_INVALID;
+    const int64_t tokens = total_tokens(p);
+    const bool gates = io->gate_a != nullptr, norm = io->norm_z != nullptr;
+    if (gates && (g != nullptr || beta != nullptr || io->gate_b == nullptr ||
+                  io->a_log == nullptr || io->dt_bias == nullptr ||
+                  (io->gate_dtype != GDR_DTYPE_F32 && io->gate_dtype != GDR_DTYPE_BF16) ||
+                  ((reinterpret_cast<uintptr_t>(io->gate_a) |
+                    reinterpret_cast<uintptr_t>(io->gate_b)) & 3)))
+        return GDR_ERR_INVALID;
+    if (norm && (io->norm_weight == nullptr || !(io->norm_eps >= 0.0) ||
+                 (reinterpret_cast<uintptr_t>(io->norm_z) & 15)))
+        return GDR_ERR_INVALID;
+    const float* g_chk = gates ? static_cast<const float*>(io->gate_a) : g;
+    const float* b_chk = gates ? static_cast<const float*>(io->gate_b) : beta;
+    if (!io_ok(p, q, k, v, g_chk, b_chk, out, state_pool)) return GDR_ERR_INVALID;
+    if (p.n_seqs > 0 && n_slots <= 0) return GDR_ERR_INVALID;
+    if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 3) != 0 ||
+        workspace_bytes < gdr::mixed_workspace_bytes(p.n_seqs))
+        return GDR_ERR_INVALID;
+    if (!gdr::chunked_tc_supports(*params)) return GDR_ERR_UNSUPPORTED;
+    if (static_cast<int64_t>(p.n_seqs) * p.heads_v >= (int64_t{1} << 30)) return GDR_ERR_UNSUPPORTED;
+    if (p.n_seqs == 0 || tokens == 0) return GDR_OK;
+    if (gates) {
+        p.gate_a = io->gate_a;
+        p.gate_b = io->gate_b;
+        p.a_log = io->a_log;
+        p.dt_bias = io->dt_bias;
+        p.gate_bf16 = io->gate_dtype == GDR_DTYPE_BF16;
+    }
+    if (norm) {
+        p.norm_z = io->norm_z;
+        p.norm_w = io->norm_weight;
+        p.norm_eps = static_cast<float>(io->norm_eps);
+    }
+    return from_cuda(gdr::launch_mixed_tc(p, q, k, v, g, beta, state_pool, state_slots, n_slots,
+                                          out, static_cast<int32_t*>(workspace),
+                                          static_cast<cudaStream_t>(stream)));
+}
+
 gdr_status gdr_mixed_noalloc(const gdr_params* params, const void* q, const void* k,
                              const void* v, const float* g, const float* beta, float* state_pool,
                              const int32_t* state_slots, int32_t n_slots, void* out,

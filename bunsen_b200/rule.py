@@ -37,6 +37,36 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _layer_io(gates, norm, q, v, g, beta):
+    """The ``gdr_layer_io`` of a call's ``gates=(a, b, a_log, dt_bias)`` and
+    ``norm=(z, weight, eps)``, the tensors it points at (kept alive by the
+    caller), and the g / beta stand-ins for the shape contract."""
+    io, keep = _lib.GdrLayerIO(), []
+    if gates is not None:
+        if g is not None or beta is not None:
+            raise ValueError("with gates=(a, b, a_log, dt_bias), g and beta are None")
+        a, b, a_log, dt_bias = gates
+        if a.dtype not in _DTYPES or b.dtype != a.dtype:
+            raise TypeError("the gate projections a, b share one dtype, f32 or bf16")
+        a, b = a.contiguous(), b.contiguous()
+        a_log = a_log.to(torch.float32).contiguous()
+        dt_bias = dt_bias.to(torch.float32).contiguous()
+        keep += [a, b, a_log, dt_bias]
+        io.gate_a, io.gate_b = a.data_ptr(), b.data_ptr()
+        io.a_log, io.dt_bias = a_log.data_ptr(), dt_bias.data_ptr()
+        io.gate_dtype = _DTYPES[a.dtype]
+        g, beta = a, b  # for the shape contract only
+    if norm is not None:
+        z, weight, eps = norm
+        if tuple(z.shape) != tuple(v.shape) or z.dtype != q.dtype:
+            raise ValueError("the norm's gate z is shaped and typed like v and out")
+        z = z.contiguous()
+        weight = weight.to(torch.float32).contiguous()
+        keep += [z, weight]
+        io.norm_z, io.norm_weight, io.norm_eps = z.data_ptr(), weight.data_ptr(), float(eps)
+    return io, keep, g, beta
+
+
 @dataclasses.dataclass(frozen=True)
 class GatedDeltaRule:
     """The rule's options (``delta_rule.rs:52-60``); the default is bunsen's
@@ -74,12 +104,16 @@ class GatedDeltaRule:
                          gates, norm)
 
     def mixed(self, q, k, v, g, beta, state_pool, *, cu_seqlens, state_slots=None, out=None,
-              workspace=None):
+              workspace=None, gates=None, norm=None):
         """A continuous batch in one launch (``gdr_mixed``): the packed batch's
         length-1 sequences step as decode rows (``recurrent``), longer ones run
         as prefill segments (``chunked``). Sequence ``s`` updates its state in
-        place at ``state_pool[state_slots[s]]``. Returns ``out``."""
+        place at ``state_pool[state_slots[s]]``. Returns ``out``. ``gates`` and
+        ``norm`` as for ``chunked`` (``gdr_mixed_layer``)."""
         assert self.chunk_size > 0, "a chunk of at least one position"
+        io, keep = None, []
+        if gates is not None or norm is not None:
+            io, keep, g, beta = _layer_io(gates, norm, q, v, g, beta)
         check_shapes(q, k, v, g, beta, None, cu_seqlens)
         dev = q.device
         if dev.type != "cuda":
@@ -89,8 +123,9 @@ class GatedDeltaRule:
         h_v, d_k, d_v = v.shape[-2], q.shape[-1], v.shape[-1]
         if tuple(state_pool.shape[1:]) != (h_v, d_k, d_v):
             raise ValueError(f"the state pool is [n_slots, {h_v}, {d_k}, {d_v}]")
-        g = g.to(torch.float32).contiguous()
-        beta = beta.to(torch.float32).contiguous()
+        if gates is None:
+            g = g.to(torch.float32).contiguous()
+            beta = beta.to(torch.float32).contiguous()
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         cu_seqlens = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
         if state_slots is not None:
@@ -102,9 +137,19 @@ class GatedDeltaRule:
         need = lib.gdr_mixed_workspace_size(ctypes.byref(p))
         if workspace is None:
             workspace = torch.empty(max(need, 4), dtype=torch.uint8, device=dev)
+        gp = None if gates is not None else g.data_ptr()
+        bp = None if gates is not None else beta.data_ptr()
+        if io is not None:
+            status = lib.gdr_mixed_layer(
+                ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), gp, bp,
+                ctypes.byref(io), state_pool.data_ptr(), _ptr(state_slots), state_pool.shape[0],
+                out.data_ptr(), cu_seqlens.data_ptr(), workspace.data_ptr(),
+                workspace.numel() * workspace.element_size(), _stream(dev))
+            _lib.check("gdr_mixed_layer", status)
+            return out
         status = lib.gdr_mixed(
-            ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
-            beta.data_ptr(), state_pool.data_ptr(), _ptr(state_slots), state_pool.shape[0],
+            ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), gp, bp,
+            state_pool.data_ptr(), _ptr(state_slots), state_pool.shape[0],
             out.data_ptr(), cu_seqlens.data_ptr(), workspace.data_ptr(),
             workspace.numel() * workspace.element_size(), _stream(dev))
         _lib.check("gdr_mixed", status)
@@ -185,29 +230,7 @@ class GatedDeltaRule:
         lead = 1 if packed else 2
         io, keep = None, []
         if gates is not None or norm is not None:
-            io = _lib.GdrLayerIO()
-            if gates is not None:
-                if g is not None or beta is not None:
-                    raise ValueError("with gates=(a, b, a_log, dt_bias), g and beta are None")
-                a, b, a_log, dt_bias = gates
-                if a.dtype not in _DTYPES or b.dtype != a.dtype:
-                    raise TypeError("the gate projections a, b share one dtype, f32 or bf16")
-                a, b = a.contiguous(), b.contiguous()
-                a_log = a_log.to(torch.float32).contiguous()
-                dt_bias = dt_bias.to(torch.float32).contiguous()
-                keep += [a, b, a_log, dt_bias]
-                io.gate_a, io.gate_b = a.data_ptr(), b.data_ptr()
-                io.a_log, io.dt_bias = a_log.data_ptr(), dt_bias.data_ptr()
-                io.gate_dtype = _DTYPES[a.dtype]
-                g, beta = a, b  # for the shape contract only
-            if norm is not None:
-                z, weight, eps = norm
-                if tuple(z.shape) != tuple(v.shape) or z.dtype != q.dtype:
-                    raise ValueError("the norm's gate z is shaped and typed like v and out")
-                z = z.contiguous()
-                weight = weight.to(torch.float32).contiguous()
-                keep += [z, weight]
-                io.norm_z, io.norm_weight, io.norm_eps = z.data_ptr(), weight.data_ptr(), float(eps)
+            io, keep, g, beta = _layer_io(gates, norm, q, v, g, beta)
         check_shapes(q, k, v, g, beta, state, cu_seqlens)
         if q.dtype not in _DTYPES:
             raise TypeError(f"q, k, v in f32 or bf16, not {q.dtype}")

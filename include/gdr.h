@@ -205,6 +205,15 @@ gdr_status gdr_gated_norm(int64_t rows, int32_t width, const void* x, const void
                           const float* weight, double eps, int32_t dtype, void* out,
                           void* stream);
 
+/* gdr_mixed with the layer's gates and gated norm, fused into its prefill
+ * segments and decode rows (io as for gdr_chunked_layer; NULL: gdr_mixed). */
+gdr_status gdr_mixed_layer(const gdr_params* params, const void* q, const void* k,
+                           const void* v, const float* g, const float* beta,
+                           const gdr_layer_io* io, float* state_pool,
+                           const int32_t* state_slots, int32_t n_slots, void* out,
+                           const int32_t* cu_seqlens, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 /* DeltaNetState::reorder (state.rs:112-135) on device: row r of dst becomes row
  * sources[r] of src, for `rows` rows of row_bytes bytes (a multiple of 4);
  * sources is device memory; src and dst must not overlap. A source outside

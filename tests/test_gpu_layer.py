@@ -174,3 +174,41 @@ def test_layer0_one_position_at_a_time(golden, name):
         norm=(z, T(d["norm_w"]), float(d["norm_eps"])))
     _ok()
     assert rel_err(_np(out).reshape(-1, dv), d["norm_out"]) < TOL_F32
+
+
+def test_mixed_batch_with_gates_and_norm_matches_separate_calls():
+    """gdr_mixed_layer: the continuous batch with the layer's gates and norm
+    equals the layer calls on its prefill segments and decode rows (the same
+    fused kernels run both)."""
+    from tests.test_gpu_mixed import _batch
+    lens = [200, 1, 1, 70, 1]
+    x = _batch(lens)
+    t = sum(lens)
+    gen = torch.Generator(device=DEV).manual_seed(51)
+    hv = x["v"].shape[-2]
+    a = torch.randn(t, hv, device=DEV, generator=gen).bfloat16()
+    b = torch.randn(t, hv, device=DEV, generator=gen).bfloat16()
+    a_log = torch.log(torch.rand(hv, device=DEV, generator=gen) * 0.3 + 0.01)
+    dt_bias = torch.randn(hv, device=DEV, generator=gen) * 0.1
+    z = torch.randn(t, hv, 128, device=DEV, generator=gen).bfloat16()
+    w = torch.rand(128, device=DEV, generator=gen) + 0.5
+    pool0 = x["pool"].clone()
+    out = GatedDeltaRule().mixed(x["q"], x["k"], x["v"], None, None, x["pool"],
+                                 cu_seqlens=x["cu_seqlens"], state_slots=x["slots"],
+                                 gates=(a, b, a_log, dt_bias), norm=(z, w, 1e-6))
+    _ok()
+    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias))
+    cu = _np(x["cu_seqlens"]).astype(np.int64)
+    slots = _np(x["slots"]).astype(np.int64)
+    from oracle import oracle
+    for s_, (lo, hi) in enumerate(zip(cu[:-1], cu[1:])):
+        if hi == lo:
+            continue
+        args = [_np(x[key][lo:hi])[None] for key in ("q", "k", "v")]
+        st0 = _np(pool0[slots[s_]])[None]
+        fn = oracle.recurrent if hi - lo == 1 else oracle.chunked
+        core, st = fn(*args, g[lo:hi][None], beta[lo:hi][None], st0)
+        want = olayer.gated_norm(_np(torch.from_numpy(core).bfloat16()), _np(z[lo:hi])[None],
+                                 _np(w), 1e-6)
+        assert rel_err(_np(out[lo:hi])[None], want) < TOL_BF16_OUT
+        assert rel_err(_np(x["pool"][slots[s_]])[None], st) < TOL_BF16_STATE
