@@ -1480,14 +1480,32 @@ split_pass(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 // X_{p+1} = M_p X_p + B_p for p = 1 .. P-2 of every split sequence and value
 // head, a block of kScanCols state columns per item (the columns of S evolve
 // independently); CTAs pull items, the longest chains first. M_p is staged
-// whole in shared memory by cp.async (every copy in flight at once), rows
-// padded to 132 floats (16-byte copies; the eight rows a warp reads fall in
-// distinct banks). Thread t accumulates rows t / 4 and t / 4 + 64, columns
-// 8 (t % 4) .. + 7 of the block, in f32.
+// whole in shared memory by cp.async (every copy in flight at once). The
+// product runs on the tensor cores as tf32 m16n8k8 mma.sync in three parts,
+// hi.hi + hi.lo + lo.hi with x = hi + lo split to tf32 (the split keeps about
+// f32 accuracy): warp w computes rows 16 w .. 16 w + 15 of the block's 32
+// columns. Rows of M_p are padded to 132 floats and of the state block to 40,
+// so each fragment load meets 32 distinct banks.
 constexpr int kScanCols = kD / kScanBlocks;
 constexpr int kScanPad = kD + 4;
-constexpr uint32_t kScanSmem = (kD * kScanPad + kD * kScanCols) * 4;
-static_assert(kScanCols == 32, "thread layout: 64 row pairs x 4 groups of 8 columns");
+constexpr int kScanSPad = kScanCols + 8;
+constexpr uint32_t kScanSmem = (kD * kScanPad + kD * kScanSPad) * 4;
+static_assert(kScanCols == 32, "four n-tiles of 8 columns per warp");
+
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+    const float r = x - __uint_as_float(hi);
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(r));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 __global__ void __launch_bounds__(256, 2)
 split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H) {
     extern __shared__ float ssm[];
@@ -1496,7 +1514,8 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
     __shared__ int item;
     const int n_items = work[4] * H * kScanBlocks;
     if (static_cast<int>(blockIdx.x) >= n_items) return;
-    const int tid = threadIdx.x, r0 = tid >> 2, r1 = r0 + 64, cg = 8 * (tid & 3);
+    const int tid = threadIdx.x, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+    const int rw = 16 * (tid >> 5);  // this warp's first row
     auto copy16 = [](float* dst, const float* src) {
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                      : "memory");
@@ -1517,7 +1536,7 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
             const float* x1 = split_state(scratch, seg_cap, H, 0, base + 1, h);
             for (int e = tid; e < kD * kScanCols / 4; e += blockDim.x) {
                 const int row = e / (kScanCols / 4), c4 = e % (kScanCols / 4);
-                copy16(Ss + row * kScanCols + 4 * c4, x1 + row * kD + col0 + 4 * c4);
+                copy16(Ss + row * kScanSPad + 4 * c4, x1 + row * kD + col0 + 4 * c4);
             }
         }
 #pragma unroll 1
@@ -1530,47 +1549,48 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
                 copy16(Ms + row * kScanPad + c, m + 4 * e);
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
-            const float* bp = split_state(scratch, seg_cap, H, 1, base + j, h) + col0 + cg;
-            float a0[8], a1[8];
-            {
-                const float4* b0 = reinterpret_cast<const float4*>(bp + r0 * kD);
-                const float4* b1 = reinterpret_cast<const float4*>(bp + r1 * kD);
-                const float4 u0 = b0[0], u1 = b0[1], w0 = b1[0], w1 = b1[1];
-                a0[0] = u0.x, a0[1] = u0.y, a0[2] = u0.z, a0[3] = u0.w;
-                a0[4] = u1.x, a0[5] = u1.y, a0[6] = u1.z, a0[7] = u1.w;
-                a1[0] = w0.x, a1[1] = w0.y, a1[2] = w0.z, a1[3] = w0.w;
-                a1[4] = w1.x, a1[5] = w1.y, a1[6] = w1.z, a1[7] = w1.w;
+            // C starts as B_p: fragment (row rw + gq (+8), column 8 nt + 2 tq (+1)).
+            const float* bp = split_state(scratch, seg_cap, H, 1, base + j, h) + col0;
+            float c[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const float2 u = *reinterpret_cast<const float2*>(bp + (rw + gq) * kD + 8 * nt + 2 * tq);
+                const float2 v = *reinterpret_cast<const float2*>(bp + (rw + gq + 8) * kD + 8 * nt + 2 * tq);
+                c[nt][0] = u.x, c[nt][1] = u.y, c[nt][2] = v.x, c[nt][3] = v.y;
             }
             asm volatile("cp.async.wait_group 0;" ::: "memory");
             __syncthreads();
-            const float* m0 = Ms + r0 * kScanPad;
-            const float* m1 = Ms + r1 * kScanPad;
-#pragma unroll 4
-            for (int kk = 0; kk < kD; ++kk) {
-                const float x0 = m0[kk], x1 = m1[kk];
-                const float4 s0 = reinterpret_cast<const float4*>(Ss + kk * kScanCols + cg)[0];
-                const float4 s1 = reinterpret_cast<const float4*>(Ss + kk * kScanCols + cg)[1];
-                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll 2
+            for (int ks = 0; ks < kD / 8; ++ks) {
+                const float* ma = Ms + (rw + gq) * kScanPad + 8 * ks + tq;
+                uint32_t ah[4], al[4];
+                tf32_split(ma[0], ah[0], al[0]);
+                tf32_split(ma[8 * kScanPad], ah[1], al[1]);
+                tf32_split(ma[4], ah[2], al[2]);
+                tf32_split(ma[8 * kScanPad + 4], ah[3], al[3]);
+                const float* sb = Ss + (8 * ks + tq) * kScanSPad + gq;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    a0[c] = fmaf(x0, sv[c], a0[c]);
-                    a1[c] = fmaf(x1, sv[c], a1[c]);
+                for (int nt = 0; nt < 4; ++nt) {
+                    uint32_t bh0, bl0, bh1, bl1;
+                    tf32_split(sb[8 * nt], bh0, bl0);
+                    tf32_split(sb[4 * kScanSPad + 8 * nt], bh1, bl1);
+                    mma_tf32(c[nt], ah, bh0, bh1);
+                    mma_tf32(c[nt], ah, bl0, bl1);
+                    mma_tf32(c[nt], al, bh0, bh1);
                 }
             }
             __syncthreads();  // every read of Ss and Ms is done
-            float* xn = split_state(scratch, seg_cap, H, 0, base + j + 1, h) + col0 + cg;
-            const float4 o00 = make_float4(a0[0], a0[1], a0[2], a0[3]);
-            const float4 o01 = make_float4(a0[4], a0[5], a0[6], a0[7]);
-            const float4 o10 = make_float4(a1[0], a1[1], a1[2], a1[3]);
-            const float4 o11 = make_float4(a1[4], a1[5], a1[6], a1[7]);
-            reinterpret_cast<float4*>(Ss + r0 * kScanCols + cg)[0] = o00;
-            reinterpret_cast<float4*>(Ss + r0 * kScanCols + cg)[1] = o01;
-            reinterpret_cast<float4*>(Ss + r1 * kScanCols + cg)[0] = o10;
-            reinterpret_cast<float4*>(Ss + r1 * kScanCols + cg)[1] = o11;
-            reinterpret_cast<float4*>(xn + r0 * kD)[0] = o00;
-            reinterpret_cast<float4*>(xn + r0 * kD)[1] = o01;
-            reinterpret_cast<float4*>(xn + r1 * kD)[0] = o10;
-            reinterpret_cast<float4*>(xn + r1 * kD)[1] = o11;
+            float* xn = split_state(scratch, seg_cap, H, 0, base + j + 1, h) + col0;
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const int cc = 8 * nt + 2 * tq;
+                const float2 top = make_float2(c[nt][0], c[nt][1]);
+                const float2 bot = make_float2(c[nt][2], c[nt][3]);
+                *reinterpret_cast<float2*>(Ss + (rw + gq) * kScanSPad + cc) = top;
+                *reinterpret_cast<float2*>(Ss + (rw + gq + 8) * kScanSPad + cc) = bot;
+                *reinterpret_cast<float2*>(xn + (rw + gq) * kD + cc) = top;
+                *reinterpret_cast<float2*>(xn + (rw + gq + 8) * kD + cc) = bot;
+            }
             __syncthreads();
         }
         __syncthreads();
