@@ -397,6 +397,38 @@ gdr_status gdr_state_reorder(const void* src, void* dst, const int32_t* sources,
 
 namespace {
 
+// The checks of a gdr_layer_io every layer call shares (the buffers' own
+// alignment needs are the caller's): gates need g and beta absent and their
+// four inputs, the norm its weight and a non-negative epsilon.
+gdr_status check_layer_io(const gdr_layer_io& io, int64_t tokens, const float* g,
+                          const float* beta) {
+    if (io.gate_a != nullptr) {
+        if (g != nullptr || beta != nullptr) return GDR_ERR_INVALID;
+        if (io.gate_dtype != GDR_DTYPE_F32 && io.gate_dtype != GDR_DTYPE_BF16)
+            return GDR_ERR_INVALID;
+        if (tokens > 0 && (io.gate_b == nullptr || io.a_log == nullptr || io.dt_bias == nullptr))
+            return GDR_ERR_INVALID;
+    }
+    if (io.norm_z != nullptr &&
+        ((tokens > 0 && io.norm_weight == nullptr) || !(io.norm_eps >= 0.0)))
+        return GDR_ERR_INVALID;
+    return GDR_OK;
+}
+
+// The fused steps' inputs into the kernels' descriptor.
+void set_layer_gates(const gdr_layer_io& io, Problem& p) {
+    p.gate_a = io.gate_a;
+    p.gate_b = io.gate_b;
+    p.a_log = io.a_log;
+    p.dt_bias = io.dt_bias;
+    p.gate_bf16 = io.gate_dtype == GDR_DTYPE_BF16;
+}
+void set_layer_norm(const gdr_layer_io& io, Problem& p) {
+    p.norm_z = io.norm_z;
+    p.norm_w = io.norm_weight;
+    p.norm_eps = static_cast<float>(io.norm_eps);
+}
+
 // A rule call with the layer's gates and gated norm. The tensor-core prefill
 // (single pass or split) and the recurrent kernels produce g and beta from
 // the projections as they stage them, and the tensor-core prefill and the
@@ -417,15 +449,7 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
     if (st != GDR_OK) return st;
     const int64_t tokens = total_tokens(p);
     const bool gates = io->gate_a != nullptr, norm = io->norm_z != nullptr;
-    if (gates) {
-        if (g != nullptr || beta != nullptr) return GDR_ERR_INVALID;
-        if (io->gate_dtype != GDR_DTYPE_F32 && io->gate_dtype != GDR_DTYPE_BF16)
-            return GDR_ERR_INVALID;
-        if (tokens > 0 && (io->gate_b == nullptr || io->a_log == nullptr || io->dt_bias == nullptr))
-            return GDR_ERR_INVALID;
-    }
-    if (norm && ((tokens > 0 && io->norm_weight == nullptr) || !(io->norm_eps >= 0.0)))
-        return GDR_ERR_INVALID;
+    if ((st = check_layer_io(*io, tokens, g, beta)) != GDR_OK) return st;
     const float* g_chk = gates ? static_cast<const float*>(io->gate_a) : g;
     const float* b_chk = gates ? static_cast<const float*>(io->gate_b) : beta;
     if (!io_ok(p, q, k, v, g_chk, b_chk, out, state_out)) return GDR_ERR_INVALID;
@@ -441,18 +465,8 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
         ((reinterpret_cast<uintptr_t>(io->gate_a) | reinterpret_cast<uintptr_t>(io->gate_b)) & 3))
         return GDR_ERR_INVALID;
     if (tc && fuse_norm && (reinterpret_cast<uintptr_t>(io->norm_z) & 15)) return GDR_ERR_INVALID;
-    if (fuse_gates) {
-        p.gate_a = io->gate_a;
-        p.gate_b = io->gate_b;
-        p.a_log = io->a_log;
-        p.dt_bias = io->dt_bias;
-        p.gate_bf16 = io->gate_dtype == GDR_DTYPE_BF16;
-    }
-    if (fuse_norm) {
-        p.norm_z = io->norm_z;
-        p.norm_w = io->norm_weight;
-        p.norm_eps = static_cast<float>(io->norm_eps);
-    }
+    if (fuse_gates) set_layer_gates(*io, p);
+    if (fuse_norm) set_layer_norm(*io, p);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* scratch = nullptr;
     const size_t gates_n = static_cast<size_t>(tokens) * p.heads_v;
@@ -555,15 +569,13 @@ gdr_status gdr_mixed_layer(const gdr_params* params, const void* q, const void* 
     if (params->chunk_size <= 0) return GDR_ERR_INVALID;
     const int64_t tokens = total_tokens(p);
     const bool gates = io->gate_a != nullptr, norm = io->norm_z != nullptr;
-    if (gates && (g != nullptr || beta != nullptr || io->gate_b == nullptr ||
-                  io->a_log == nullptr || io->dt_bias == nullptr ||
-                  (io->gate_dtype != GDR_DTYPE_F32 && io->gate_dtype != GDR_DTYPE_BF16) ||
-                  ((reinterpret_cast<uintptr_t>(io->gate_a) |
-                    reinterpret_cast<uintptr_t>(io->gate_b)) & 3)))
+    if ((st = check_layer_io(*io, tokens, g, beta)) != GDR_OK) return st;
+    // The prefill segments stage 4-byte words of the projections and read z
+    // 16 bytes at a time.
+    if (gates &&
+        ((reinterpret_cast<uintptr_t>(io->gate_a) | reinterpret_cast<uintptr_t>(io->gate_b)) & 3))
         return GDR_ERR_INVALID;
-    if (norm && (io->norm_weight == nullptr || !(io->norm_eps >= 0.0) ||
-                 (reinterpret_cast<uintptr_t>(io->norm_z) & 15)))
-        return GDR_ERR_INVALID;
+    if (norm && (reinterpret_cast<uintptr_t>(io->norm_z) & 15)) return GDR_ERR_INVALID;
     const float* g_chk = gates ? static_cast<const float*>(io->gate_a) : g;
     const float* b_chk = gates ? static_cast<const float*>(io->gate_b) : beta;
     if (!io_ok(p, q, k, v, g_chk, b_chk, out, state_pool)) return GDR_ERR_INVALID;
@@ -574,18 +586,8 @@ gdr_status gdr_mixed_layer(const gdr_params* params, const void* q, const void* 
     if (!gdr::chunked_tc_supports(*params)) return GDR_ERR_UNSUPPORTED;
     if (static_cast<int64_t>(p.n_seqs) * p.heads_v >= (int64_t{1} << 30)) return GDR_ERR_UNSUPPORTED;
     if (p.n_seqs == 0 || tokens == 0) return GDR_OK;
-    if (gates) {
-        p.gate_a = io->gate_a;
-        p.gate_b = io->gate_b;
-        p.a_log = io->a_log;
-        p.dt_bias = io->dt_bias;
-        p.gate_bf16 = io->gate_dtype == GDR_DTYPE_BF16;
-    }
-    if (norm) {
-        p.norm_z = io->norm_z;
-        p.norm_w = io->norm_weight;
-        p.norm_eps = static_cast<float>(io->norm_eps);
-    }
+    if (gates) set_layer_gates(*io, p);
+    if (norm) set_layer_norm(*io, p);
     return from_cuda(gdr::launch_mixed_tc(p, q, k, v, g, beta, state_pool, state_slots, n_slots,
                                           out, static_cast<int32_t*>(workspace),
                                           static_cast<cudaStream_t>(stream)));

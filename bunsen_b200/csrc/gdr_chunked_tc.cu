@@ -454,7 +454,8 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
     uint32_t ph_tma = 0, ph_mma = 0, ph_qs = 0;
     auto issue_g1 = [&] {  // thread 0, once the chunk's tiles have landed
         tc_fence_after();
-        const uint32_t id = idesc_bf16(128, 128, 0, 0, 0);
+        // Without an output only the keys' Gram (columns 0-63) is read.
+        const uint32_t id = idesc_bf16(128, with_out ? 128 : 64, 0, 0, 0);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
@@ -490,7 +491,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         // (e) This thread's 32 Gram columns, and the norms from the diagonal.
         float gr[32];
         tmem_ld32(lane_addr + kColG + 32 * hf, gr);
-        if (qd >= 2 && hf == 0) {
+        if (with_out && qd >= 2 && hf == 0) {
             float dq[32];
             tmem_ld32(lane_addr + kColG + 32 * qd, dq);  // q_i . q_i at column 64 + i
             tmem_wait_ld();
@@ -519,9 +520,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             const float eg = __expf(gt);
             ms.wk[tid] = ms.bet[tid] * eg * ms.fk[tid];
             ms.rr[tid] = __expf(last - gt) * ms.fk[tid];
-            ms.cq[tid] = eg * ms.fq[tid];
+            if constexpr (with_out) ms.cq[tid] = eg * ms.fq[tid];
         }
-        {
+        if (with_out || qd < 2) {  // without an output, no intra rows
             const bool key_row = qd < 2;
             const int i = key_row ? row : row - kC;
             // This warp's 32 x 32 block of rows (i) and columns (j): below the
@@ -1165,6 +1166,7 @@ struct SplitDesc {
 // (0: nothing split), [7] the scan's cursor.
 constexpr int kSplitHeader = 16;
 constexpr int kSplitCands = 16;        // segment lengths the plan tries
+constexpr int kPlanCache = 4096;       // sequences whose chunk counts the plan keeps
 // Costs in chunk-times (one chunk of one item with every CTA slot busy),
 // fitted to B200 timings of both passes and the scan at 4 to 32 value heads.
 constexpr float kItemCost = 0.5f;       // per item: state in and out, setup
@@ -1243,16 +1245,22 @@ plan_split(const Problem p, int32_t* work, SplitDesc* da, SplitDesc* db, int4* s
     auto cand = [&](int i) {
         return forced > 0 ? forced : static_cast<int>(l_min * __powf(1.15f, static_cast<float>(i)));
     };
-    auto chunks_of = [&](int s) {
+    // Chunk counts, read from the offsets once and kept for the first
+    // kPlanCache sequences (the three passes below read them again).
+    __shared__ int ccache[kPlanCache];
+    auto chunks_global = [&](int s) {
         int64_t a, b;
         seq_span(p, s, a, b);
         return static_cast<int>((b - a + kC - 1) / kC);
     };
+    auto chunks_of = [&](int s) { return s < kPlanCache ? ccache[s] : chunks_global(s); };
     auto bucket = [&](int c) {  // descending chunk count
         return kPlanBuckets - 1 - (c < kPlanBuckets - 1 ? c : kPlanBuckets - 1);
     };
     for (int i = tid; i < kPlanBuckets; i += blockDim.x) hist[0][i] = hist[1][i] = hist[2][i] = 0;
+    for (int i = tid; i < n && i < kPlanCache; i += blockDim.x) ccache[i] = chunks_global(i);
     if (tid == 0) n_split = n_slot = 0;
+    __syncthreads();
     // Warp i scores candidate i (warp kSplitCands: no split), lanes over the
     // sequences, then one warp reduction.
     if (warp <= kSplitCands && (warp < n_cand || warp == kSplitCands)) {

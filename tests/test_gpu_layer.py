@@ -212,3 +212,42 @@ def test_mixed_batch_with_gates_and_norm_matches_separate_calls():
                                  _np(w), 1e-6)
         assert rel_err(_np(out[lo:hi])[None], want) < TOL_BF16_OUT
         assert rel_err(_np(x["pool"][slots[s_]])[None], st) < TOL_BF16_STATE
+
+
+def test_mixer_steps_in_parts_agree_with_one_pass():
+    """gated_delta_net.rs:495-523 after the projections: the layer's conv,
+    gates, rule and norm run in parts [0, 4), [4, 5), [5, 9) through the conv
+    and recurrent states (the one-position part as a decode step) equal the
+    one pass, outputs and final states (f32, within 1e-4)."""
+    gen = torch.Generator(device=DEV).manual_seed(71)
+    b, t, hk, hv, dk, dv, taps = 2, 9, 2, 4, 8, 8, 4
+    c = 2 * hk * dk + hv * dv
+    f = dict(device=DEV, generator=gen)
+    mixed = torch.randn(b, t, c, **f)
+    wconv = torch.randn(c, taps, **f) * 0.5
+    a, bb = torch.randn(b, t, hv, **f), torch.randn(b, t, hv, **f)
+    a_log, dt_bias = torch.randn(hv, **f) * 0.5, torch.randn(hv, **f) * 0.1
+    z, nw = torch.randn(b, t, hv, dv, **f), torch.rand(dv, **f) + 0.5
+    rule = GatedDeltaRule(chunk_size=4)
+
+    def layer(sl, conv_state, rec_state):
+        (q, k, v), conv_next = causal_conv1d(mixed[:, sl].contiguous(), wconv, conv_state,
+                                             silu=True, splits=(hk * dk, 2 * hk * dk))
+        n = q.shape[1]
+        q, k, v = q.reshape(b, n, hk, dk), k.reshape(b, n, hk, dk), v.reshape(b, n, hv, dv)
+        form = rule.recurrent if n == 1 else rule.chunked
+        out, rec_next = form(q, k, v, None, None, rec_state,
+                             gates=(a[:, sl].contiguous(), bb[:, sl].contiguous(), a_log,
+                                    dt_bias),
+                             norm=(z[:, sl].contiguous(), nw, 1e-6))
+        return out, conv_next, rec_next
+
+    whole, conv1, rec1 = layer(slice(0, t), None, None)
+    conv_s, rec_s, parts = None, None, []
+    for lo, hi in ((0, 4), (4, 5), (5, 9)):
+        out, conv_s, rec_s = layer(slice(lo, hi), conv_s, rec_s)
+        parts.append(out)
+    _ok()
+    assert rel_err(_np(torch.cat(parts, 1)), _np(whole)) < TOL_F32
+    assert rel_err(_np(conv_s), _np(conv1)) < TOL_F32
+    assert rel_err(_np(rec_s), _np(rec1)) < TOL_F32

@@ -48,3 +48,30 @@ def test_cpu_tensors_are_refused():
     q = _x(1, 2, 1, 4)
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         GatedDeltaRule().chunked(q, q, q, _x(1, 2, 1), _x(1, 2, 1))
+
+
+def test_layer_options_are_checked_before_the_device():
+    """gates replace g and beta; the norm's gate is shaped and typed like v;
+    both are refused on the host when malformed."""
+    q = _x(1, 5, 2, 4)
+    v = _x(1, 5, 4, 6)
+    a = _x(1, 5, 4)
+    gates = (a, a, _x(4), _x(4))
+    with pytest.raises(ValueError, match="g and beta are None"):
+        GatedDeltaRule().chunked(q, q, v, a, a, gates=gates)
+    with pytest.raises(TypeError, match="share one dtype"):
+        GatedDeltaRule().chunked(q, q, v, None, None, gates=(a, a.double(), _x(4), _x(4)))
+    with pytest.raises(ValueError, match="shaped and typed like v"):
+        GatedDeltaRule().chunked(q, q, v, a, a, norm=(_x(1, 5, 4, 5), _x(6), 1e-6))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        GatedDeltaRule().chunked(q, q, v, None, None, gates=gates, norm=(v, _x(6), 1e-6))
+
+
+def test_layer_module_refuses_host_tensors():
+    from bunsen_b200.layer import causal_conv1d, gated_norm, state_reorder
+    with pytest.raises(RuntimeError, match="CUDA"):
+        causal_conv1d(_x(1, 4, 8), _x(8, 4))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gated_norm(_x(3, 8), _x(3, 8), _x(8), 1e-6)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        state_reorder(_x(3, 8), torch.zeros(3, dtype=torch.int32))
