@@ -616,12 +616,13 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         tc_fence_before();
         fence_proxy_async();
         __syncthreads();
-        // (m) G3: R1 += -(S^T W^T) (R1 = -(S^T W^T) when U = 0), committed
-        //     alone so (n) starts while R0 = S^T Q^T runs (committed to bar_qs).
+        // (m) G3: R1 += -(S^T W^T) (R1 = -(S^T W^T) when U = 0), issued by
+        //     thread 0 and committed alone so (n) starts while R0 = S^T Q^T
+        //     runs; that half is issued by thread 32 (committed to bar_qs), so
+        //     neither issuing thread waits on the other's MMAs.
         if (tid == 0) {
             tc_fence_after();
             const uint32_t id_w = idesc_bf16(128, 64, 0, 1, 1);
-            const uint32_t id_q = idesc_bf16(128, 64, 0, 0, 0);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
                 const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
@@ -629,6 +630,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                           !zero_v || ks > 0);
             }
             umma_commit(&ms.bar_mma);
+        } else if (tid == 32) {
+            tc_fence_after();
+            const uint32_t id_q = idesc_bf16(128, 64, 0, 0, 0);
             if constexpr (with_out) {
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
@@ -685,7 +689,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         // (p) The next chunk's gates (this chunk's are no longer read).
         if (warp == 0 && ci + 1 < n_chunks) put_gates();
         wait(&ms.bar_mma, ph_mma);
-        wait(&ms.bar_qs, ph_qs);  // done with the G4/G5 group before it
+        wait(&ms.bar_qs, ph_qs);
         tc_fence_after();
         // (r) The next chunk's tiles load while this chunk's output is written.
         //     With the gated norm, this chunk's z rows land in the tail of ST
