@@ -148,15 +148,20 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
                  : "r"(addr));
 }
 
-// c[nt] (two 16 x 8 tiles) += A B for the 16 x 16 blocks A at (ar, ac) of tile
-// `ta` and B at (br, bc) of tile `tb` (B stored [k][n]), bf16 operands through
-// ldmatrix, f32 accumulation (mma.sync m16n8k16).
-__device__ __forceinline__ void mma16_bf16(uint32_t ta, int ar, int ac, uint32_t tb, int br,
-                                           int bc, float (&c)[2][4], int lane) {
+// Fragments of mma.sync m16n8k16 (bf16 operands, f32 accumulators) for 16 x 16
+// blocks of the 64 x 64 swizzled tiles: A (row-major) at (r0, c0) of `tile`,
+// B stored [k][n] at (r0, c0); c[nt] covers columns 8 nt .. 8 nt + 7.
+__device__ __forceinline__ void frag_a(uint32_t (&a)[4], uint32_t tile, int r0, int c0, int lane) {
     const int i = lane >> 3, j = lane & 7;
-    uint32_t a[4], b[4];
-    ldsm_x4(a, ta + sw_off(ar + j + 8 * (i & 1), ac + 8 * (i >> 1)));
-    ldsm_x4_trans(b, tb + sw_off(br + j + 8 * (i & 1), bc + 8 * (i >> 1)));
+    ldsm_x4(a, tile + sw_off(r0 + j + 8 * (i & 1), c0 + 8 * (i >> 1)));
+}
+__device__ __forceinline__ void frag_b(uint32_t (&b)[4], uint32_t tile, int r0, int c0, int lane) {
+    const int i = lane >> 3, j = lane & 7;
+    ldsm_x4_trans(b, tile + sw_off(r0 + j + 8 * (i & 1), c0 + 8 * (i >> 1)));
+}
+// c += A B.
+__device__ __forceinline__ void mma16(float (&c)[2][4], const uint32_t (&a)[4],
+                                      const uint32_t (&b)[4]) {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
         asm volatile(
@@ -164,6 +169,14 @@ __device__ __forceinline__ void mma16_bf16(uint32_t ta, int ar, int ac, uint32_t
             "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
             : "+f"(c[nt][0]), "+f"(c[nt][1]), "+f"(c[nt][2]), "+f"(c[nt][3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[2 * nt]), "r"(b[2 * nt + 1]));
+}
+// An accumulator block as the A operand of the next product (bf16): the
+// m16n8 accumulator layout of two column tiles is the m16k16 A layout.
+__device__ __forceinline__ void acc_to_a(uint32_t (&a)[4], const float (&c)[2][4]) {
+    a[0] = pack_bf16(c[0][0], c[0][1]);
+    a[1] = pack_bf16(c[0][2], c[0][3]);
+    a[2] = pack_bf16(c[1][0], c[1][1]);
+    a[3] = pack_bf16(c[1][2], c[1][3]);
 }
 
 // sign * c as bf16 at the 16 x 16 block (r0, c0) of a tile; with `fac`, each
@@ -187,26 +200,28 @@ constexpr uint32_t kLdStride = 17;                        // f32 diagonal blocks
 constexpr uint32_t kOffLd = 0;                            // 4 x 16 x 17 f32
 constexpr uint32_t kOffLb = 8192;                         // L, bf16 64 x 64
 constexpr uint32_t kOffXb = kOffLb + 8192;                // A, bf16 64 x 64
-constexpr uint32_t kOffNb = kOffXb + 8192;                // the N blocks, bf16
 
-// A = (I + L)^-1 for the strictly lower 64 x 64 L, in 16 x 16 blocks:
-//  D  the diagonal blocks X_ii = (I + L_ii)^-1, exact f32 forward
-//     substitution from `Ld` (f32, the four diagonal blocks of L);
-//  N  N_ij = X_ii L_ij for the six blocks below the diagonal;
-//  then X_ij = -sum_{k=j}^{i-1} N_ik X_kj, one block diagonal per level,
-//  each product issued as soon as its X_kj exists, so three levels of one
-//  product each follow N. Products are bf16 mma.sync with f32 accumulation
-//  on `Lb` (L in bf16). Every block of A goes out, as it is found, as bf16 to
-//  `Xb` (for the later levels) and scaled by the column factors fac0 / fac1
-//  to the two G2 operands at AB and AB + kTileBytes, which get their zero
-//  blocks above the diagonal here too.
+// A = (I + L)^-1 for the strictly lower 64 x 64 L, in 16 x 16 blocks X_ij:
+//  the diagonal blocks X_ii = (I + L_ii)^-1 by exact f32 forward substitution
+//  from `Ld` (f32, the four diagonal blocks of L); then, for the two 32 x 32
+//  halves lo = {0, 1} and hi = {2, 3}, X_hi,lo = -X_hi L_hi,lo X_lo:
+//   step 1  X_10 = -(X_11 L_10) X_00, X_32 = -(X_33 L_32) X_22,
+//           X_21 = -(X_22 L_21) X_11, and the parts of P = X_hi L_hi,lo
+//           that need only diagonal blocks;
+//   step 2  P_3k += X_32 L_2k; X_20, X_30 = -(P_i0 X_00 + P_i1 X_10),
+//           X_31 = -P_31 X_11.
+//  Products are bf16 mma.sync with f32 accumulation on `Lb` (L in bf16) and
+//  `Xb` (the blocks later products read); a product's result feeds the next
+//  one from registers, rounded to bf16. Every block of A goes out as it is
+//  found, scaled by the column factors fac0 / fac1, to the two G2 operands at
+//  AB and AB + kTileBytes, which get their zero blocks above the diagonal
+//  here too.
 __device__ void unit_lower_inverse_64(uint8_t* ST, int tid, const float* fac0, const float* fac1,
                                       uint8_t* AB) {
     const int warp = tid >> 5, lane = tid & 31;
     const float* Ld = reinterpret_cast<const float*>(ST + kOffLd);
     uint8_t* Xb = ST + kOffXb;
-    uint8_t* Nb = ST + kOffNb;
-    const uint32_t sLb = smem_u32(ST + kOffLb), sXb = smem_u32(Xb), sNb = smem_u32(Nb);
+    const uint32_t sLb = smem_u32(ST + kOffLb), sXb = smem_u32(Xb);
     uint8_t* Au = AB;
     uint8_t* Aw = AB + kTileBytes;
     if (tid < 64) {
@@ -240,43 +255,58 @@ __device__ void unit_lower_inverse_64(uint8_t* ST, int tid, const float* fac0, c
         }
     }
     __syncthreads();
-    // Block pairs (i, j) of N, by warp: (1,0) (2,1) (3,2) (2,0) (3,1) (3,0).
-    const int pi = warp < 3 ? warp + 1 : (warp < 5 ? warp - 1 : 3);
-    const int pj = warp < 3 ? warp : (warp < 5 ? warp - 3 : 0);
-    if (warp < 6) {
-        float c[2][4] = {};
-        mma16_bf16(sXb, 16 * pi, 16 * pi, sLb, 16 * pi, 16 * pj, c, lane);
-        store16_bf16(Nb, 16 * pi, 16 * pj, c, 1.f, nullptr, lane);
-    }
-    __syncthreads();
-    // Level 1: X_10, X_21, X_32; and the parts of X_20, X_31, X_30 that only
-    // need diagonal blocks.
-    float c[2][4] = {};
-    auto put = [&](int i, int j, bool keep) {  // X_ij = -c
+    auto put = [&](int i, int j, const float (&c)[2][4], bool keep) {  // X_ij = -c
         if (keep) store16_bf16(Xb, 16 * i, 16 * j, c, -1.f, nullptr, lane);
         store16_bf16(Au, 16 * i, 16 * j, c, -1.f, fac0, lane);
         store16_bf16(Aw, 16 * i, 16 * j, c, -1.f, fac1, lane);
     };
-    if (warp < 6) {
-        mma16_bf16(sNb, 16 * pi, 16 * pj, sXb, 16 * pj, 16 * pj, c, lane);  // N_ij X_jj
-        if (warp < 3) put(pi, pj, warp < 2);  // X_10, X_21 feed level 2
+    uint32_t a[4], b[4];
+    float p0[2][4] = {}, p1[2][4] = {};  // P_i0, P_i1 of warps 3 .. 5
+    if (warp < 3) {
+        // Step 1: X_10 (warp 0), X_32 (warp 1), X_21 (warp 2) = -(X_ii L_ij) X_jj.
+        const int i = warp == 0 ? 1 : (warp == 1 ? 3 : 2), j = i - 1;
+        frag_a(a, sXb, 16 * i, 16 * i, lane);
+        frag_b(b, sLb, 16 * i, 16 * j, lane);
+        mma16(p0, a, b);
+        acc_to_a(a, p0);
+        frag_b(b, sXb, 16 * j, 16 * j, lane);
+        float x[2][4] = {};
+        mma16(x, a, b);
+        put(i, j, x, warp < 2);  // X_10 and X_32 are read by step 2
+    } else if (warp < 6) {
+        // Step 1: P_20, P_21 = X_22 L_2k (warp 3); P_30, P_31 (warp 4) and
+        // P_31 (warp 5) start as X_33 L_3k.
+        const int i = warp == 3 ? 2 : 3;
+        frag_a(a, sXb, 16 * i, 16 * i, lane);
+        if (warp < 5) {
+            frag_b(b, sLb, 16 * i, 0, lane);
+            mma16(p0, a, b);
+        }
+        frag_b(b, sLb, 16 * i, 16, lane);
+        mma16(p1, a, b);
     }
     __syncthreads();
-    // Level 2: X_20 += N_21 X_10, X_31 += N_32 X_21; X_30 gathers N_31 X_10.
-    if (warp == 3) {
-        mma16_bf16(sNb, 32, 16, sXb, 16, 0, c, lane);
-        put(2, 0, true);
-    } else if (warp == 4) {
-        mma16_bf16(sNb, 48, 32, sXb, 32, 16, c, lane);
-        put(3, 1, false);
-    } else if (warp == 5) {
-        mma16_bf16(sNb, 48, 16, sXb, 16, 0, c, lane);
-    }
-    __syncthreads();
-    // Level 3: X_30 += N_32 X_20.
-    if (warp == 5) {
-        mma16_bf16(sNb, 48, 32, sXb, 32, 0, c, lane);
-        put(3, 0, false);
+    if (warp >= 3 && warp < 6) {
+        // Step 2.
+        if (warp > 3) {  // P_3k += X_32 L_2k
+            frag_a(a, sXb, 48, 32, lane);
+            if (warp == 4) {
+                frag_b(b, sLb, 32, 0, lane);
+                mma16(p0, a, b);
+            }
+            frag_b(b, sLb, 32, 16, lane);
+            mma16(p1, a, b);
+        }
+        float x[2][4] = {};
+        if (warp < 5) {  // P_i0 X_00
+            acc_to_a(a, p0);
+            frag_b(b, sXb, 0, 0, lane);
+            mma16(x, a, b);
+        }
+        acc_to_a(a, p1);  // P_i1 X_10 (X_20, X_30) or P_31 X_11 (X_31)
+        frag_b(b, sXb, 16, warp == 5 ? 16 : 0, lane);
+        mma16(x, a, b);
+        put(warp == 3 ? 2 : 3, warp == 5 ? 1 : 0, x, false);
     }
 }
 
