@@ -228,7 +228,10 @@ def cpu_sample(w: workloads.Workload, max_tokens: int = 8192, heads_v: int = 8):
     x = workloads.make_inputs(sw, "cpu", seed=99)
     f = {k: workloads.to_numpy_f32(v) for k, v in x.items() if k != "cu_seqlens"}
     cu = x["cu_seqlens"].numpy().astype(np.int32)
-    threads = oracle.max_threads()
+    # Every core this process may run on: a launcher's OMP_NUM_THREADS (torchrun
+    # sets 1 per rank) is not the host's thread budget for the one CPU run.
+    threads = (len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
+               else oracle.max_threads())
 
     def run():
         oracle.chunked(f["q"], f["k"], f["v"], f["g"], f["beta"], f["state"], cu_seqlens=cu,
