@@ -786,7 +786,10 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         }
         if constexpr (with_out) {
             if (p.norm_z == nullptr) {
-                for (int e = tid; e < valid * 16; e += kThreads) {
+                // Warp 0 issues the next chunk's G1 and leaves these stores to
+                // the other warps, so the next chunk does not wait on its share.
+                const int first = ci + 1 < n_chunks ? 32 : 0;
+                for (int e = tid - first; e >= 0 && e < valid * 16; e += kThreads - first) {
                     const int t = e >> 4, c = e & 15;
                     const uint4* src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2) + c;
                     uint4* dst =
