@@ -1210,7 +1210,7 @@ constexpr float kItemCost = 0.5f;       // per item: state in and out, setup
 constexpr float kAloneFactor = 0.75f;   // a chunk when at most one CTA per SM is busy
 constexpr float kScanStepCost = 1.1f;   // one link of the longest scan chain
 constexpr float kScanLaunchCost = 1.0f;
-constexpr int kScanBlocks = 4;          // column blocks of a (sequence, head) scan
+constexpr int kScanBlocks = 8;          // column blocks of a (sequence, head) scan
 
 // A pass of `n` items (`work` chunk-times in all, the longest `longest`) on
 // `slots` CTA slots, as the longest-first list schedule runs it: one wave
@@ -1528,14 +1528,18 @@ split_pass(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 // whole in shared memory by cp.async (every copy in flight at once). The
 // product runs on the tensor cores as tf32 m16n8k8 mma.sync in three parts,
 // hi.hi + hi.lo + lo.hi with x = hi + lo split to tf32 (the split keeps about
-// f32 accuracy): warp w computes rows 16 w .. 16 w + 15 of the block's 32
-// columns. Rows of M_p are padded to 132 floats and of the state block to 40,
-// so each fragment load meets 32 distinct banks.
+// f32 accuracy): warp w computes rows 16 w .. 16 w + 15 of the block's 16
+// columns. Rows of M_p are padded to 132 floats and of the state block to 24,
+// so each fragment load meets 32 distinct banks. Eight 16-column blocks per
+// (sequence, head) measured faster than four of 32 (the chain of links is the
+// longest item; its work per link halves, its load of M_p does not) and than
+// sixteen of 8.
 constexpr int kScanCols = kD / kScanBlocks;
 constexpr int kScanPad = kD + 4;
 constexpr int kScanSPad = kScanCols + 8;
 constexpr uint32_t kScanSmem = (kD * kScanPad + kD * kScanSPad) * 4;
-static_assert(kScanCols == 32, "four n-tiles of 8 columns per warp");
+constexpr int kScanNT = kScanCols / 8;  // n-tiles of 8 columns per warp
+static_assert(kScanCols % 8 == 0, "whole n-tiles");
 
 __device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
@@ -1596,9 +1600,9 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
             asm volatile("cp.async.commit_group;" ::: "memory");
             // C starts as B_p: fragment (row rw + gq (+8), column 8 nt + 2 tq (+1)).
             const float* bp = split_state(scratch, seg_cap, H, 1, base + j, h) + col0;
-            float c[4][4];
+            float c[kScanNT][4];
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
+            for (int nt = 0; nt < kScanNT; ++nt) {
                 const float2 u = *reinterpret_cast<const float2*>(bp + (rw + gq) * kD + 8 * nt + 2 * tq);
                 const float2 v = *reinterpret_cast<const float2*>(bp + (rw + gq + 8) * kD + 8 * nt + 2 * tq);
                 c[nt][0] = u.x, c[nt][1] = u.y, c[nt][2] = v.x, c[nt][3] = v.y;
@@ -1615,7 +1619,7 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
                 tf32_split(ma[8 * kScanPad + 4], ah[3], al[3]);
                 const float* sb = Ss + (8 * ks + tq) * kScanSPad + gq;
 #pragma unroll
-                for (int nt = 0; nt < 4; ++nt) {
+                for (int nt = 0; nt < kScanNT; ++nt) {
                     uint32_t bh0, bl0, bh1, bl1;
                     tf32_split(sb[8 * nt], bh0, bl0);
                     tf32_split(sb[4 * kScanSPad + 8 * nt], bh1, bl1);
@@ -1627,7 +1631,7 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
             __syncthreads();  // every read of Ss and Ms is done
             float* xn = split_state(scratch, seg_cap, H, 0, base + j + 1, h) + col0;
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
+            for (int nt = 0; nt < kScanNT; ++nt) {
                 const int cc = 8 * nt + 2 * tq;
                 const float2 top = make_float2(c[nt][0], c[nt][1]);
                 const float2 bot = make_float2(c[nt][2], c[nt][3]);
