@@ -149,8 +149,10 @@ cudaError_t host_streams(cudaStream_t** out) {
     if (!made[dev]) {
         for (int i = 0; i < kHostStreams; ++i)
             if ((e = cudaStreamCreateWithFlags(&streams[dev][i], cudaStreamNonBlocking)) !=
-                cudaSuccess)
+                cudaSuccess) {
+                while (i-- > 0) cudaStreamDestroy(streams[dev][i]);  // next call starts over
                 return e;
+            }
         made[dev] = true;
     }
     *out = streams[dev];

@@ -1840,11 +1840,15 @@ cudaError_t library_pool(cudaMemPool_t* pool) {
         props.allocType = cudaMemAllocationTypePinned;
         props.location.type = cudaMemLocationTypeDevice;
         props.location.id = dev;
-        if ((e = cudaMemPoolCreate(&pools[dev], &props)) != cudaSuccess) return e;
+        cudaMemPool_t made = nullptr;
+        if ((e = cudaMemPoolCreate(&made, &props)) != cudaSuccess) return e;
         uint64_t keep = UINT64_MAX;
-        if ((e = cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep)) !=
-            cudaSuccess)
+        if ((e = cudaMemPoolSetAttribute(made, cudaMemPoolAttrReleaseThreshold, &keep)) !=
+            cudaSuccess) {
+            cudaMemPoolDestroy(made);  // a later call tries again from scratch
             return e;
+        }
+        pools[dev] = made;
     }
     *pool = pools[dev];
     return cudaSuccess;
