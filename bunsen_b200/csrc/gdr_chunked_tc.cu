@@ -829,9 +829,9 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const float y0 =
-                                x[2 * j] * r * wv[2 * j] * silu_f32(__bfloat162float(zb[2 * j]));
+                                x[2 * j] * r * wv[2 * j] * silu_bf16(__bfloat162float(zb[2 * j]));
                             const float y1 = x[2 * j + 1] * r * wv[2 * j + 1] *
-                                             silu_f32(__bfloat162float(zb[2 * j + 1]));
+                                             silu_bf16(__bfloat162float(zb[2 * j + 1]));
                             yw[j] = pack_bf16(y0, y1);
                         }
                         *reinterpret_cast<uint4*>(out + row) = y;

@@ -104,4 +104,13 @@ __device__ __forceinline__ void rule_gates(const Problem& p, const float* g, con
 // x sigmoid(x) with the fast exponential and divide (0 for very negative x).
 __device__ __forceinline__ float silu_f32(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
+// silu for bf16 results: x sigmoid(x) = h + h tanh(h), h = x / 2, with the
+// one-instruction tanh (relative error near 5e-4, below bf16's 4e-3 step).
+__device__ __forceinline__ float silu_bf16(float x) {
+    const float h = 0.5f * x;
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+    return fmaf(h, t, h);
+}
+
 }  // namespace gdr
