@@ -726,11 +726,12 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         //     (free once the Q S group is done), each thread copying the row
         //     pieces it normalises in (s).
         if (tid == 0 && ci + 1 < n_chunks) issue_tiles(ci + 1);
+        // Warp 0 issues the next chunk's G1 and leaves the output rows to the
+        // other warps (`lead` threads skipped), here and in (s).
+        const int lead = ci + 1 < n_chunks ? 32 : 0;
         if (with_out && p.norm_z != nullptr) {
-            const int c = tid & 15;
-#pragma unroll
-            for (int u = 0; u < kC / 16; ++u) {
-                const int t = (tid >> 4) + 16 * u;
+            for (int e = tid - lead; e >= 0 && e < kC * 16; e += kThreads - lead) {
+                const int t = e >> 4, c = e & 15;
                 const int tt = t < valid ? t : 0;
                 const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.norm_z) +
                                            ((tok0 + tt) * p.heads_v + h) * kD + 8 * c;
@@ -786,10 +787,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
         }
         if constexpr (with_out) {
             if (p.norm_z == nullptr) {
-                // Warp 0 issues the next chunk's G1 and leaves these stores to
-                // the other warps, so the next chunk does not wait on its share.
-                const int first = ci + 1 < n_chunks ? 32 : 0;
-                for (int e = tid - first; e >= 0 && e < valid * 16; e += kThreads - first) {
+                for (int e = tid - lead; e >= 0 && e < valid * 16; e += kThreads - lead) {
                     const int t = e >> 4, c = e & 15;
                     const uint4* src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2) + c;
                     uint4* dst =
@@ -806,7 +804,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 const float4 w1 = reinterpret_cast<const float4*>(p.norm_w)[2 * cw + 1];
                 const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll 1
-                for (int e = tid; e < kC * 16; e += kThreads) {
+                for (int e = tid - lead; e >= 0 && e < kC * 16; e += kThreads - lead) {
                     const int t = e >> 4, c = e & 15;
                     const bool in = t < valid;
                     const uint4 src = reinterpret_cast<const uint4*>(ST + t * kOsStride * 2)[c];
