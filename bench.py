@@ -18,9 +18,15 @@ counts the pack's tokens (all heads) once -- strong scaling. `--verify`
 gathers the sharded outputs (NCCL all_gather, outside the timed region) and
 compares them with an unsharded run on rank 0.
 
-`--impl reference` times the CPU oracle -- a C++ restatement of bunsen's burn
-rule (the reference itself is Rust and cannot be built here), OpenMP over all
-host threads -- on a bounded sample of the same ragged workload.
+`cpu_baseline` (rank 0, one GPU) and `--impl reference` time the CPU oracle --
+a C++ restatement of bunsen's burn rule (the reference itself is Rust and
+cannot be built here), OpenMP over (sequence, head) pairs on every host core
+the process may use -- on the whole of each workload: the ragged pack (the
+reference arm's step), the dense batch, one decode step and the mixed batch.
+
+`roofline` is the attainable roof of one call, max(FLOPs / bf16 tensor peak,
+bytes / HBM bandwidth), with the burst tensor peak (timed regions here last
+tens of milliseconds) and the measured peaks of MEASURED_PEAKS.json.
 """
 
 from __future__ import annotations
@@ -75,32 +81,40 @@ def prefill_bytes(w: workloads.Workload, heads_qk: int, heads_v: int) -> float:
 
 
 def measured_traffic(tokens_heads: float) -> float | None:
-    """DRAM bytes of one prefill launch over `tokens_heads` token-heads, scaled
-    from the ncu capture recorded in profiles/traffic.json."""
+    """DRAM bytes of one prefill call over `tokens_heads` token-heads, scaled
+    from the ncu capture recorded in profiles/traffic.json (every launch of
+    one call of the default path, summed)."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
-    rec = json.loads(p.read_text()).get("chunked_tc")
+    rec = json.loads(p.read_text()).get("ragged_prefill_call")
     if not rec:
         return None
     return rec["dram_bytes"] / rec["token_heads"] * tokens_heads
 
 
 def roofline(flops: float, nbytes: float, kern_ms: float, pk: dict, pk_kind: str,
-             traffic: float | None) -> dict:
-    """The binding roof (sustained tensor or HBM) for this launch and the
-    fraction of it achieved."""
-    t_flop = flops / (pk["bf16_tflops_sustained"] * 1e12)
+             traffic: float | None, tensor_peak: str = "burst") -> dict:
+    """The attainable roof of one call, t_min = max(FLOPs / tensor peak, bytes /
+    HBM bandwidth), names the binding roof (`bound`); `frac` = t_min / the
+    measured time, which is the achieved rate over that roof's peak. The
+    tensor peak is the burst figure for calls timed in a region well under a
+    second, the sustained one for long regions."""
+    tc = pk["bf16_tflops"] if tensor_peak == "burst" else pk["bf16_tflops_sustained"]
+    t_flop = flops / (tc * 1e12)
     t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
     s = kern_ms * 1e-3
     if t_flop >= t_hbm:
-        out = {"bound": "tensor", "achieved": flops / s / 1e12, "peak": pk["bf16_tflops_sustained"],
-               "unit": "TFLOP/s"}
+        out = {"bound": "tensor", "achieved": flops / s / 1e12, "peak": tc, "unit": "TFLOP/s"}
     else:
-        out = {"bound": "hbm", "achieved": nbytes / s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
+        out = {"bound": "hbm", "achieved": nbytes / s / 1e9, "peak": pk["hbm_gbs"],
+               "unit": "GB/s"}
     out["frac"] = out["achieved"] / out["peak"]
-    out.update(traffic=traffic, peak_source=pk_kind, flops_per_launch=flops,
-               bytes_per_launch=nbytes, tflops=flops / s / 1e12, gbs=nbytes / s / 1e9)
+    out.update(traffic=traffic, peak_source=f"{pk_kind} ({tensor_peak} tensor peak)",
+               attainable_ms=1e3 * max(t_flop, t_hbm), measured_ms=kern_ms,
+               flops_per_launch=flops, bytes_per_launch=nbytes,
+               tflops=flops / s / 1e12, gbs=nbytes / s / 1e9,
+               tensor_frac=flops / s / 1e12 / tc, hbm_frac=nbytes / s / 1e9 / pk["hbm_gbs"])
     return out
 
 
@@ -209,58 +223,105 @@ def timed(step, k: int, w: int, dist: Dist, stream) -> tuple[float, list[float]]
     return dist.max(evs[0].elapsed_time(evs[-1])), per
 
 
-# -- the CPU baseline -----------------------------------------------------------------
-def cpu_sample(w: workloads.Workload, max_tokens: int = 8192, heads_v: int = 8):
-    """A bounded sample of the ragged pack for the CPU oracle: its first
-    sequences up to `max_tokens` tokens, at `heads_v` of the value heads.
-    Returns (run, token-equivalents of the full-head workload, description)."""
+# -- the CPU baseline ------------------------------------------------------------
+# The oracle (a C++ restatement of bunsen's burn rule, OpenMP over (sequence,
+# head) pairs) on the host's cores, on the same workloads as the GPU legs.
+def cpu_threads() -> int:
+    """Every core this process may run on: a launcher's OMP_NUM_THREADS
+    (torchrun sets 1 per rank) is not the host's thread budget for the one
+    CPU run."""
     from oracle import oracle
 
-    lens, tot = [], 0
-    for L in w.seqlens:
-        if tot + L > max_tokens and lens:
-            break
-        lens.append(L)
-        tot += L
-    heads_qk = heads_v * w.heads_qk // w.heads_v
-    sw = workloads.Workload("sample", tuple(lens), heads_qk, heads_v, w.d_k, w.d_v, w.chunk,
-                            w.dtype, True, True)
-    x = workloads.make_inputs(sw, "cpu", seed=99)
+    return (len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
+            else oracle.max_threads())
+
+
+def cpu_inputs(name: str, seed: int = 99) -> tuple[workloads.Workload, dict]:
+    """A workload's inputs as f32 numpy arrays on the host (bf16 values
+    widened exactly, as bunsen widens them)."""
+    w = workloads.get(name)
+    x = workloads.make_inputs(w, "cpu", seed=seed)
     f = {k: workloads.to_numpy_f32(v) for k, v in x.items() if k != "cu_seqlens"}
-    cu = x["cu_seqlens"].numpy().astype(np.int32)
-    # Every core this process may run on: a launcher's OMP_NUM_THREADS (torchrun
-    # sets 1 per rank) is not the host's thread budget for the one CPU run.
-    threads = (len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
-               else oracle.max_threads())
-
-    def run():
-        oracle.chunked(f["q"], f["k"], f["v"], f["g"], f["beta"], f["state"], cu_seqlens=cu,
-                       chunk_size=w.chunk, threads=threads)
-
-    desc = (f"{len(lens)} sequences / {tot} tokens of the pack at {heads_v} of {w.heads_v} value "
-            f"heads (f32 chunked oracle, {threads} threads); scaled to all heads")
-    return run, tot * heads_v / w.heads_v, desc, threads
+    if "cu_seqlens" in x:
+        f["cu_seqlens"] = x["cu_seqlens"].numpy().astype(np.int32)
+    return w, f
 
 
-def cpu_baseline(w: workloads.Workload, seconds: float = 15.0) -> dict:
-    run, tok, desc, threads = cpu_sample(w)
+def cpu_runner(name: str, threads: int):
+    """(workload, one run of the whole workload on the oracle, what it is)."""
+    from oracle import oracle
+
+    w, f = cpu_inputs(name)
+    args = lambda sl=slice(None): [f[k][sl] for k in ("q", "k", "v", "g", "beta")]  # noqa: E731
+    if name in ("ragged_prefill", "dense_prefill"):
+        def run():
+            oracle.chunked(*args(), f.get("state"), cu_seqlens=f.get("cu_seqlens"),
+                           chunk_size=w.chunk, threads=threads)
+        what = "f32 chunked oracle"
+    elif name == "decode":
+        def run():
+            oracle.recurrent(*args(), f["state"], threads=threads)
+        what = "f32 recurrent oracle, one step"
+    elif name == "mixed":
+        n_pre = sum(1 for L in w.seqlens if L > 1)
+        t_pre = sum(L for L in w.seqlens if L > 1)
+        cu = f["cu_seqlens"][:n_pre + 1]
+        pre, dec = args(slice(0, t_pre)), [a[:, None] for a in args(slice(t_pre, None))]
+
+        def run():
+            oracle.chunked(*pre, f["state"][:n_pre], cu_seqlens=cu, chunk_size=w.chunk,
+                           threads=threads)
+            oracle.recurrent(*dec, f["state"][n_pre:], threads=threads)
+        what = "f32 chunked oracle on the prefill segments + recurrent on the decode rows"
+    else:
+        raise KeyError(name)
+    return w, run, f"the whole {name} workload ({what}, {threads} threads)"
+
+
+def time_cpu(run, seconds: float) -> tuple[float, int]:
+    """Mean seconds per run: at least one run, more until `seconds` pass."""
     t0 = time.perf_counter()
     reps = 0
     while reps < 1 or (time.perf_counter() - t0 < seconds and reps < 100):
         run()
         reps += 1
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": tok / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{desc}; {reps} reps"}
+    return (time.perf_counter() - t0) / reps, reps
+
+
+def cpu_baselines(seconds: float = 5.0) -> dict:
+    """The oracle on every workload of the GPU legs, in the GPU legs' units."""
+    threads = cpu_threads()
+    res = {}
+    for name in ("ragged_prefill", "dense_prefill", "decode", "mixed"):
+        w, run, desc = cpu_runner(name, threads)
+        dt, reps = time_cpu(run, seconds)
+        base = {"cores": threads, "kind": "port", "sample": f"{desc}; {reps} runs"}
+        if name == "decode":
+            state_rw = 2.0 * w.n_seqs * w.heads_v * w.d_k * w.d_v * 4
+            res[name] = {"value": state_rw / dt / 1e9, "unit": "GB/s", **base}
+        elif name == "mixed":
+            res[name] = {"value": 1e3 * dt, "unit": "ms", "higher_is_better": False, **base}
+        else:
+            res[name] = {"value": w.tokens / dt, "unit": "tokens/s", **base}
+        del run
+    return res
+
+
+def headline_config(w: workloads.Workload, world: int) -> dict:
+    """The `config` of the headline line, the same in both arms."""
+    return {"workload": "ragged_prefill", "tokens": w.tokens, "n_seqs": w.n_seqs,
+            "max_len": max(w.seqlens), "heads_qk": w.heads_qk, "heads_v": w.heads_v,
+            "d": w.d_k, "chunk": w.chunk, "parallelism": f"heads{world}",
+            "l2": "inputs larger than L2 (no flush)"}
 
 
 def run_reference(args, dist: Dist) -> None:
-    """The reference arm: the oracle's chunked form on the host's cores, one
-    bounded sample per step, on rank 0 only."""
+    """The reference arm: the oracle's chunked form over the whole ragged
+    workload on all the host's cores, one run per step, on rank 0 only."""
     if dist.rank != 0:
         return
-    w = workloads.get("ragged_prefill")
-    run, tok, desc, threads = cpu_sample(w)
+    threads = cpu_threads()
+    w, run, desc = cpu_runner("ragged_prefill", threads)
     for _ in range(args.warmup):
         run()
     per = []
@@ -269,14 +330,12 @@ def run_reference(args, dist: Dist) -> None:
         run()
         per.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(per)
-    tok_s = tok / (ms * 1e-3)
+    tok_s = w.tokens / (ms * 1e-3)
     line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "ragged_prefill", "tokens": w.tokens, "n_seqs": w.n_seqs,
-                       "heads_qk": w.heads_qk, "heads_v": w.heads_v, "d": w.d_k,
-                       "chunk": w.chunk},
+            "config": headline_config(w, args.gpus),
             "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads,
                              "kind": "port", "sample": desc},
             "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -545,25 +604,23 @@ def run_native(args, dist: Dist) -> None:
     layer = bench_layer(args, dist, dev, stream, pk, pk_kind)
     if lib.gdr_device_error() != _lib.GDR_OK:
         raise RuntimeError("a kernel recorded a device-side failure")
-    cpu = None
+    cpu = {}
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(workloads.get("ragged_prefill"))
+        cpu = cpu_baselines()
     if dist.rank == 0:
         w = workloads.get("ragged_prefill")
+        dense = {k: dense[k] for k in ("value", "unit", "ms_per_step", "roofline", "clocks")}
+        dense["cpu_baseline"] = cpu.get("dense_prefill")
+        decode["cpu_baseline"] = cpu.get("decode")
+        mixed["cpu_baseline"] = cpu.get("mixed")
         line = {"metric": METRIC, "value": rag["value"], "unit": "tokens/s",
                 "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": rag["ms_per_step"], "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "ragged_prefill", "tokens": w.tokens, "n_seqs": w.n_seqs,
-                           "max_len": max(w.seqlens), "heads_qk": w.heads_qk,
-                           "heads_v": w.heads_v, "d": w.d_k, "chunk": w.chunk,
-                           "parallelism": f"heads{dist.world}",
-                           "l2": "inputs larger than L2 (no flush)"},
-                "roofline": rag["roofline"], "cpu_baseline": cpu, "e2e": rag["e2e"],
-                "gpu_launches": rag["gpu_launches"], "clocks": rag["clocks"],
-                "dense": {k: dense[k] for k in ("value", "unit", "ms_per_step", "roofline",
-                                                "clocks")},
-                "decode": decode, "mixed": mixed, "layer": layer}
+                "config": headline_config(w, dist.world),
+                "roofline": rag["roofline"], "cpu_baseline": cpu.get("ragged_prefill"),
+                "e2e": rag["e2e"], "gpu_launches": rag["gpu_launches"], "clocks": rag["clocks"],
+                "dense": dense, "decode": decode, "mixed": mixed, "layer": layer}
         if "verified" in rag:
             line["verified"] = rag["verified"]
         print(json.dumps(line), flush=True)

@@ -88,6 +88,7 @@ SIGNATURES = {
     "gdr_mixed_noalloc": (_i32, [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i32, _vp, _vp, _vp]),
     "gdr_selftest_wait_timeout": (_i32, [ctypes.c_int64, _vp]),
+    "gdr_release_scratch": (_i32, []),
     "gdr_device_error": (_i32, []),
     "gdr_status_string": (ctypes.c_char_p, [_i32]),
     "gdr_abi_version": (_i32, []),

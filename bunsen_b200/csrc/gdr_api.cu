@@ -25,7 +25,7 @@ cudaError_t launch_chunked_split(const Problem&, const void*, const void*, const
                                  cudaStream_t);
 cudaError_t take_device_error(int* flag);
 cudaError_t take_layer_error(int* flag);
-cudaError_t library_pool(cudaMemPool_t* pool);
+cudaError_t library_pool(cudaMemPool_t* pool, bool create);
 int conv_max_taps();
 cudaError_t launch_causal_conv1d(int dtype, int32_t n_seqs, int64_t tokens, int32_t seq_len,
                                  const int32_t* cu_seqlens, int32_t channels, int32_t taps,
@@ -274,29 +274,31 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
     cudaStream_t* ws = nullptr;
     cudaMemPool_t pool;
     cudaError_t e = host_streams(&ws);
-    if (e == cudaSuccess) e = gdr::library_pool(&pool);
+    if (e == cudaSuccess) e = gdr::library_pool(&pool, true);
     void* mem = nullptr;
     if (e == cudaSuccess) e = cudaMallocFromPoolAsync(&mem, bytes, pool, caller);
     if (e != cudaSuccess) return GDR_ERR_CUDA;
     uint8_t* base = static_cast<uint8_t*>(mem);
     int32_t* cu_all = reinterpret_cast<int32_t*>(base + o_all);
-    auto ok = [&](cudaError_t x) {
-        if (e == cudaSuccess) e = x;
-    };
+    // Each CUDA call below runs only while every earlier one succeeded.
+#define GDR_TRY(call)                      \
+    do {                                   \
+        if (e == cudaSuccess) e = (call);  \
+    } while (0)
     if (packed)
-        ok(cudaMemcpyAsync(cu_all, cu_seqlens, (static_cast<size_t>(n) + 1) * 4,
-                           cudaMemcpyHostToDevice, caller));
-    cudaEvent_t start, done[kHostStreams];
-    ok(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
+        GDR_TRY(cudaMemcpyAsync(cu_all, cu_seqlens, (static_cast<size_t>(n) + 1) * 4,
+                                cudaMemcpyHostToDevice, caller));
+    cudaEvent_t start = nullptr, done[kHostStreams] = {};
+    GDR_TRY(cudaEventCreateWithFlags(&start, cudaEventDisableTiming));
     for (int w = 0; w < kHostStreams; ++w)
-        ok(cudaEventCreateWithFlags(&done[w], cudaEventDisableTiming));
-    ok(cudaEventRecord(start, caller));
-    for (int w = 0; w < kHostStreams; ++w) ok(cudaStreamWaitEvent(ws[w], start, 0));
+        GDR_TRY(cudaEventCreateWithFlags(&done[w], cudaEventDisableTiming));
+    GDR_TRY(cudaEventRecord(start, caller));
+    for (int w = 0; w < kHostStreams; ++w) GDR_TRY(cudaStreamWaitEvent(ws[w], start, 0));
     auto h2d = [&](void* dst, const void* src, size_t len, cudaStream_t s) {
-        if (len > 0) ok(cudaMemcpyAsync(dst, src, len, cudaMemcpyHostToDevice, s));
+        if (len > 0) GDR_TRY(cudaMemcpyAsync(dst, src, len, cudaMemcpyHostToDevice, s));
     };
     auto d2h = [&](void* dst, const void* src, size_t len, cudaStream_t s) {
-        if (len > 0) ok(cudaMemcpyAsync(dst, src, len, cudaMemcpyDeviceToHost, s));
+        if (len > 0) GDR_TRY(cudaMemcpyAsync(dst, src, len, cudaMemcpyDeviceToHost, s));
     };
     const auto* hq = static_cast<const uint8_t*>(q);
     const auto* hk = static_cast<const uint8_t*>(k);
@@ -315,9 +317,9 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
         h2d(b + o_b, beta + t0 * p.heads_v, nt * row_gb, s);
         if (state_in) h2d(b + o_s, state_in + s0 * (one_state / 4), ns * one_state, s);
         int32_t* cu = reinterpret_cast<int32_t*>(b + o_c);
-        if (packed) {
+        if (packed && e == cudaSuccess) {
             rebase_offsets<<<1, 256, 0, s>>>(cu_all + s0, ns + 1, cu);
-            ok(cudaGetLastError());
+            GDR_TRY(cudaGetLastError());
         }
         gdr_params gp = *params;
         if (packed) {
@@ -335,14 +337,27 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
         d2h(ho + t0 * row_v, b + o_o, nt * row_v, s);
         d2h(state_out + s0 * (one_state / 4), ds, ns * one_state, s);
     }
+#undef GDR_TRY
     // The caller's stream waits for every worker; the scratch is freed after.
+    // Where that order could not be set up (an earlier failure), the workers
+    // are drained on the host first, so no copy still in flight can touch the
+    // scratch once the pool hands it out again.
+    bool ordered = true;
     for (int w = 0; w < kHostStreams; ++w) {
-        ok(cudaEventRecord(done[w], ws[w]));
-        ok(cudaStreamWaitEvent(caller, done[w], 0));
+        cudaError_t r = done[w] != nullptr ? cudaEventRecord(done[w], ws[w])
+                                           : cudaErrorInvalidResourceHandle;
+        if (r == cudaSuccess) r = cudaStreamWaitEvent(caller, done[w], 0);
+        if (r != cudaSuccess) {
+            ordered = false;
+            if (e == cudaSuccess) e = r;
+        }
     }
+    if (!ordered)
+        for (int w = 0; w < kHostStreams; ++w) cudaStreamSynchronize(ws[w]);
     const cudaError_t f = cudaFreeAsync(mem, caller);
-    cudaEventDestroy(start);
-    for (int w = 0; w < kHostStreams; ++w) cudaEventDestroy(done[w]);
+    if (start != nullptr) cudaEventDestroy(start);
+    for (int w = 0; w < kHostStreams; ++w)
+        if (done[w] != nullptr) cudaEventDestroy(done[w]);
     return from_cuda(e != cudaSuccess ? e : f);
 }
 
@@ -474,7 +489,7 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
     const size_t gates_n = static_cast<size_t>(tokens) * p.heads_v;
     if (gates && !fuse_gates && gates_n > 0) {
         cudaMemPool_t pool;
-        if (gdr::library_pool(&pool) != cudaSuccess ||
+        if (gdr::library_pool(&pool, true) != cudaSuccess ||
             cudaMallocFromPoolAsync(&scratch, 2 * gates_n * sizeof(float), pool, s) != cudaSuccess)
             return GDR_ERR_CUDA;
         g = static_cast<const float*>(scratch);
@@ -627,6 +642,14 @@ gdr_status gdr_device_error(void) {
     flag |= layer;
     if (flag & 1) return GDR_ERR_TIMEOUT;
     return (flag & 2) ? GDR_ERR_INVALID : GDR_OK;
+}
+
+gdr_status gdr_release_scratch(void) {
+    cudaMemPool_t pool = nullptr;
+    if (gdr::library_pool(&pool, false) != cudaSuccess) return GDR_ERR_CUDA;
+    if (pool == nullptr) return GDR_OK;  // nothing was ever taken on this device
+    if (cudaDeviceSynchronize() != cudaSuccess) return GDR_ERR_CUDA;
+    return from_cuda(cudaMemPoolTrimTo(pool, 0));
 }
 
 const char* gdr_status_string(gdr_status status) {

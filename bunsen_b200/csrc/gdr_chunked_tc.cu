@@ -12,9 +12,9 @@
 //
 //   G1  [K;Q] [K;Q]^T       -> TMEM G [128 x 128]  Gram of keys and queries
 //        (CUDA cores: norms from its diagonal, decay mask, L =
-//         strict_lower(.), intra; A = (I + L)^-1: exact 16 x 16 diagonal
-//         blocks by forward substitution, off-diagonal blocks by tf32
-//         mma.sync)
+//         strict_lower(.), intra; A = (I + L)^-1: exact f32 16 x 16 diagonal
+//         blocks by forward substitution, off-diagonal blocks by bf16
+//         ldmatrix / mma.sync with f32 accumulation)
 //   G2  V^T (A diag(beta))^T                -> R1  U^T       [d_v x C]
 //       K^T (A diag(beta e^gamma / |k|))^T  -> R0  W^T       [d_k x C]
 //        (CUDA cores, while G2 runs: S^T -> bf16 operand, S^T <- e^gamma_C
@@ -429,7 +429,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             x = __uint_as_float((__float_as_uint(x) >> ((i & 1) ? 16 : 0)) << 16);
         }
         ms.gstage[which][t] = pos >= len ? 0.f
-                              : which   ? gate_beta(x)
+                              : which   ? gate_beta(x, p.gate_bf16)
                                         : gate_g(x, p.a_log[h], p.dt_bias[h]);
     };
     // Warp 0: the staged gates into the chunk's arrays, the log decay as its
@@ -799,6 +799,11 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                 // a row's 128 features (8 each) and reduce over them; z from
                 // the rows staged at (r).
                 asm volatile("cp.async.wait_group 0;" ::: "memory");
+                // The loop below ends in full-warp shuffles, so every lane of
+                // a warp must run it equally often: kC * 16, kThreads and
+                // `lead` (0 or 32) are all multiples of the warp size.
+                static_assert((kC * 16) % 32 == 0 && kThreads % 32 == 0,
+                              "whole warps walk the output rows");
                 const int cw = tid & 15;
                 const float4 w0 = reinterpret_cast<const float4*>(p.norm_w)[2 * cw];
                 const float4 w1 = reinterpret_cast<const float4*>(p.norm_w)[2 * cw + 1];
@@ -1836,9 +1841,11 @@ constexpr size_t kSplitStateBudget = size_t{2} << 30;  // scratch states, bytes
 }  // namespace
 
 // The stream-ordered pool the library's scratch comes from (split calls,
-// host-buffer calls): one per device, owned by the library, never trimmed, so
-// repeated calls reuse its memory.
-cudaError_t library_pool(cudaMemPool_t* pool) {
+// host-buffer calls): one per device, owned by the library. Its release
+// threshold keeps freed memory reserved so repeated calls reuse it;
+// gdr_release_scratch gives it back. With create false, a device without a
+// pool yet gets a null pool.
+cudaError_t library_pool(cudaMemPool_t* pool, bool create) {
     constexpr int kMaxDevices = 64;
     static std::mutex mu;
     static cudaMemPool_t pools[kMaxDevices] = {};
@@ -1847,7 +1854,7 @@ cudaError_t library_pool(cudaMemPool_t* pool) {
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(mu);
-    if (pools[dev] == nullptr) {
+    if (pools[dev] == nullptr && create) {
         cudaMemPoolProps props = {};
         props.allocType = cudaMemAllocationTypePinned;
         props.location.type = cudaMemLocationTypeDevice;
@@ -1926,7 +1933,7 @@ cudaError_t launch_chunked_split(const Problem& p, const void* q, const void* k,
     const size_t bytes =
         off_x + 3 * static_cast<size_t>(sh.seg_cap) * p.heads_v * kD * kD * sizeof(float);
     cudaMemPool_t pool;
-    if ((e = library_pool(&pool)) != cudaSuccess) return e;
+    if ((e = library_pool(&pool, true)) != cudaSuccess) return e;
     void* mem = nullptr;
     if ((e = cudaMallocFromPoolAsync(&mem, bytes, pool, stream)) != cudaSuccess) return e;
     uint8_t* base = static_cast<uint8_t*>(mem);

@@ -75,13 +75,19 @@ __device__ __forceinline__ float l2_factor(const Problem& p, float sumsq) {
 }
 
 // The layer's gates from its projections (gated_delta_net.rs:422-426):
-// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b), in f32.
+// g = -exp(A_log) softplus(a + dt_bias) in f32 (the layer widens a, A_log and
+// dt_bias to f32 first); beta = sigmoid(b) on the projection's own tensor, so
+// its value is rounded to the projection's dtype (bf16 in a bf16 model) before
+// the rule widens it back to f32.
 __device__ __forceinline__ float gate_g(float a, float a_log, float dt_bias) {
     const float x = a + dt_bias;
     const float sp = x > 20.f ? x : log1pf(expf(x));
     return -expf(a_log) * sp;
 }
-__device__ __forceinline__ float gate_beta(float b) { return 1.f / (1.f + expf(-b)); }
+__device__ __forceinline__ float gate_beta(float b, int32_t bf16) {
+    const float s = 1.f / (1.f + expf(-b));
+    return bf16 ? __bfloat162float(__float2bfloat16_rn(s)) : s;
+}
 
 __device__ __forceinline__ float load_gate_input(const void* base, int64_t i, int32_t bf16) {
     return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
@@ -94,7 +100,7 @@ __device__ __forceinline__ void rule_gates(const Problem& p, const float* g, con
                                            int64_t i, int h, float& gi, float& bi) {
     if (p.gate_a != nullptr) {
         gi = gate_g(load_gate_input(p.gate_a, i, p.gate_bf16), p.a_log[h], p.dt_bias[h]);
-        bi = gate_beta(load_gate_input(p.gate_b, i, p.gate_bf16));
+        bi = gate_beta(load_gate_input(p.gate_b, i, p.gate_bf16), p.gate_bf16);
     } else {
         gi = g[i];
         bi = beta[i];
@@ -105,8 +111,13 @@ __device__ __forceinline__ void rule_gates(const Problem& p, const float* g, con
 __device__ __forceinline__ float silu_f32(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 // silu for bf16 results: x sigmoid(x) = h + h tanh(h), h = x / 2, with the
-// one-instruction tanh (relative error near 5e-4, below bf16's 4e-3 step).
+// one-instruction tanh, whose error is about 2^-11 of tanh itself. Below
+// x = -3, 1 + tanh(h) loses digits to cancellation (at x = -3 the result's
+// relative error is near 5e-3, the size of a bf16 step), so there the result
+// is x / (1 + e^-x) with the fast exponential instead (relative error below
+// 1e-5 until the result underflows to -0).
 __device__ __forceinline__ float silu_bf16(float x) {
+    if (x < -3.f) return silu_f32(x);
     const float h = 0.5f * x;
     float t;
     asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));

@@ -398,7 +398,7 @@ __global__ void gates_kernel(int64_t n, int heads, const T* __restrict__ a,
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int h = static_cast<int>(i % heads);
         g[i] = gate_g(to_f32(a[i]), a_log[h], dt_bias[h]);
-        beta[i] = gate_beta(to_f32(b[i]));
+        beta[i] = gate_beta(to_f32(b[i]), sizeof(T) == 2);
     }
 }
 

@@ -21,8 +21,9 @@
  *
  * Conventions
  *  - Every pointer is a device pointer (CUDA global memory), except `params`
- *    and the `gdr_mixed_plan` handle, which live on the host. Nothing here
- *    allocates device memory except where an entry point says so.
+ *    (and the other parameter structs), which live on the host, and the
+ *    buffers of gdr_chunked_host. Nothing here allocates device memory
+ *    except where an entry point says so.
  *  - `stream` is a `cudaStream_t` passed as `void*` (NULL: the legacy default
  *    stream). Every call is asynchronous on it; a returned GDR_OK means the
  *    work was enqueued, not that it finished.
@@ -287,6 +288,21 @@ gdr_status gdr_device_error(void);
  * The wait gives up, the kernel returns, and the next gdr_device_error()
  * reports GDR_ERR_TIMEOUT; the context stays usable. */
 gdr_status gdr_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
+/* Scratch memory. Split calls (GDR_ALGO_TENSOR_SPLIT, and AUTO when it
+ * splits), gdr_chunked_host and the layer calls whose gates are not fused
+ * take their device scratch from a stream-ordered pool the library owns, one
+ * per device. Freed scratch stays reserved in that pool so that the next call
+ * reuses it: up to about 2 GiB of segment states for split calls, three groups'
+ * worth of buffers for gdr_chunked_host. gdr_release_scratch returns the
+ * current device's unused pool memory to the driver: it waits for the
+ * device's outstanding work, then trims the pool (GDR_OK when the device has
+ * no pool). The next call that needs scratch reserves it again.
+ *
+ * The library keeps per-device handles for the life of the process (the pool,
+ * gdr_chunked_host's worker streams, gdr_mixed_noalloc's array address), so a
+ * cudaDeviceReset after the first call on a device is not supported. */
+gdr_status gdr_release_scratch(void);
 
 /* A short English description of a status. */
 const char* gdr_status_string(gdr_status status);

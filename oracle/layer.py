@@ -11,8 +11,11 @@ Each function follows bunsen's own code, in f32 unless stated:
   in tap order; the next state is the last ``K - 1`` inputs of the window
   ``[state, x]``. The layer then applies silu (``gated_delta_net.rs:401``) and
   splits the channels into q, k, v (``:404-420``).
-* ``gates``: ``gated_delta_net.rs:422-426``: ``beta = sigmoid(b)``,
-  ``g = -exp(A_log) * softplus(a + dt_bias)``.
+* ``gates``: ``gated_delta_net.rs:422-426``: ``g = -exp(A_log) *
+  softplus(a + dt_bias)`` in f32 (``Widening::F32`` over ``a``, ``A_log`` and
+  ``dt_bias``); ``beta = sigmoid(b)`` on the projection's own tensor, so the
+  value keeps the projection's dtype: rounded to bf16 for a bf16 model
+  (``beta_dtype="bf16"``), before the rule widens it back to f32.
 * ``gated_norm``: ``gated_delta_net.rs:439-440`` through ``GatedNorm``
   (``blocks/norm/gated_norm.rs``) and ``Gate::forward``
   (``burner/module/gate.rs:89-102``): an RMS norm over the last axis with its
@@ -68,14 +71,26 @@ def causal_conv1d(x, weight, state=None, *, cu_seqlens=None, activation=False):
     return y.reshape(x.shape), nxt
 
 
-def gates(a, b, a_log, dt_bias):
+def round_bf16(x):
+    """f32 values rounded to the nearest bf16 (ties to even), as f32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
+def gates(a, b, a_log, dt_bias, beta_dtype=None):
     """``(g, beta)`` from the projections ``a, b [..., H]`` and the per-head
-    ``A_log, dt_bias [H]``."""
+    ``A_log, dt_bias [H]``; ``beta_dtype="bf16"``: the projections are bf16
+    tensors, and beta is rounded to bf16."""
     a = np.asarray(a, dtype=np.float32)
     b = np.asarray(b, dtype=np.float32)
     sp = np.logaddexp(np.float32(0), a + np.asarray(dt_bias, np.float32)).astype(np.float32)
     g = (-np.exp(np.asarray(a_log, np.float32)) * sp).astype(np.float32)
     beta = (np.float32(1) / (np.float32(1) + np.exp(-b))).astype(np.float32)
+    if beta_dtype == "bf16":
+        beta = round_bf16(beta)
+    elif beta_dtype is not None:
+        raise ValueError(f"beta_dtype is None (f32) or 'bf16', not {beta_dtype!r}")
     return g, beta
 
 

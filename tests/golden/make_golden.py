@@ -1,11 +1,12 @@
 #!/usr/bin/env python3
 """Generate the golden vectors the oracle is pinned against.
 
-Run once in a container that has the bunsen sources mounted read-only at
-``/root/reference`` and ``transformers`` installed; commit the ``.npz`` files
-it writes next to this script. Nothing at test time reads the reference.
+Run once where the bunsen sources are readable and ``transformers`` is
+installed; commit the ``.npz`` files it writes next to this script. Nothing at
+test time reads the reference.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <bunsen checkout>
+    BUNSEN_SRC=<bunsen checkout> python tests/golden/make_golden.py
 
 Two groups of vectors are written:
 
@@ -37,7 +38,9 @@ import pathlib
 import numpy as np
 import torch
 
-REF = pathlib.Path("/root/reference/crates/public/bunsen/testdata/qwen3_5")
+# The toy fixtures' directory inside a bunsen checkout (set by main()).
+FIXTURES = "crates/public/bunsen/testdata/qwen3_5"
+REF = pathlib.Path(FIXTURES)
 OUT = pathlib.Path(__file__).resolve().parent
 
 
@@ -205,4 +208,11 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    import os
+    import sys
+
+    src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("BUNSEN_SRC")
+    if not src:
+        sys.exit("usage: make_golden.py <bunsen checkout> (or set BUNSEN_SRC)")
+    REF = pathlib.Path(src) / FIXTURES
     main()

@@ -107,7 +107,7 @@ def test_gates_and_norm_bf16_d128_against_oracle(form):
         x["q"], x["k"], x["v"], None, None, x["state"], cu_seqlens=x["cu_seqlens"],
         gates=(a, b, a_log, dt_bias), norm=(z, w, 1e-6))
     _ok()
-    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias))
+    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias), beta_dtype="bf16")
     y = dict(x, g=torch.from_numpy(g), beta=torch.from_numpy(beta))
     core, want_st = _oracle(form, y)
     core = _np(torch.from_numpy(core).bfloat16())  # the rule's output in q's dtype
@@ -149,7 +149,7 @@ def test_gates_and_norm_on_the_split_path():
         x["q"], x["k"], x["v"], None, None, x["state"], cu_seqlens=x["cu_seqlens"],
         gates=(a, b, a_log, dt_bias), norm=(z, w, 1e-6))
     _ok()
-    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias))
+    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias), beta_dtype="bf16")
     core, want_st = _oracle("chunked", dict(x, g=torch.from_numpy(g), beta=torch.from_numpy(beta)))
     want = olayer.gated_norm(_np(torch.from_numpy(core).bfloat16()), _np(z), _np(w), 1e-6)
     assert rel_err(_np(out), want) < TOL_BF16_OUT
@@ -197,7 +197,7 @@ def test_mixed_batch_with_gates_and_norm_matches_separate_calls():
                                  cu_seqlens=x["cu_seqlens"], state_slots=x["slots"],
                                  gates=(a, b, a_log, dt_bias), norm=(z, w, 1e-6))
     _ok()
-    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias))
+    g, beta = olayer.gates(_np(a), _np(b), _np(a_log), _np(dt_bias), beta_dtype="bf16")
     cu = _np(x["cu_seqlens"]).astype(np.int64)
     slots = _np(x["slots"]).astype(np.int64)
     from oracle import oracle
@@ -251,3 +251,39 @@ def test_mixer_steps_in_parts_agree_with_one_pass():
     assert rel_err(_np(torch.cat(parts, 1)), _np(whole)) < TOL_F32
     assert rel_err(_np(conv_s), _np(conv1)) < TOL_F32
     assert rel_err(_np(rec_s), _np(rec1)) < TOL_F32
+
+
+def test_conv_silu_elementwise_over_the_negative_range():
+    """The conv's bf16 silu element by element over x in [-20, 4] (a
+    two-tap filter (0, 1) passes x through): within 1e-2 of f32 silu(x)
+    relative to each element, the bf16 rounding of the result included."""
+    x = torch.linspace(-20.0, 4.0, 4096, device=DEV).bfloat16().reshape(-1, 64)
+    w = torch.zeros(64, 2, device=DEV, dtype=torch.bfloat16)
+    w[:, 1] = 1.0
+    y, _ = causal_conv1d(x[None], w, silu=True)
+    _ok()
+    xf = _np(x)
+    want = xf / (1.0 + np.exp(-xf.astype(np.float64)))
+    got = _np(y)[0]
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-2 * np.abs(want)), float((err / np.maximum(np.abs(want), 1e-30)).max())
+
+
+def test_fused_norm_elementwise_against_the_plain_prefill():
+    """The tensor-core prefill's fused gated norm against the same kernel's
+    plain output normalised on the host, element by element, with z over
+    [-20, 4]: the fused silu(z) and the row norm within 1e-2 of each element."""
+    x = _rand_bf16([200, 70], state=True, seed=61)
+    t = 270
+    gen = torch.Generator(device=DEV).manual_seed(62)
+    z = (torch.rand(t, 4, 128, device=DEV, generator=gen) * 24.0 - 20.0).bfloat16()
+    w = torch.rand(128, device=DEV, generator=gen) + 0.5
+    rule = GatedDeltaRule(algo="tensor")
+    plain, _ = rule.chunked(x["q"], x["k"], x["v"], x["g"], x["beta"], x["state"],
+                            cu_seqlens=x["cu_seqlens"])
+    fused, _ = rule.chunked(x["q"], x["k"], x["v"], x["g"], x["beta"], x["state"],
+                            cu_seqlens=x["cu_seqlens"], norm=(z, w, 1e-6))
+    _ok()
+    want = olayer.gated_norm(_np(plain), _np(z), _np(w), 1e-6)
+    err = np.abs(_np(fused) - want)
+    assert np.all(err <= 1e-2 * np.abs(want) + 1e-6), float(err.max())

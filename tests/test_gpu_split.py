@@ -73,3 +73,16 @@ def test_split_state_in_place_and_repeatable():
     torch.cuda.synchronize()
     assert got.data_ptr() == st.data_ptr()
     assert (_np(out) == o1).all() and (_np(st) == s1).all()
+
+
+def test_release_scratch_and_run_again():
+    """gdr_release_scratch returns the pool's unused memory; the next split
+    call reserves it again and gives the same bits."""
+    from bunsen_b200 import _lib
+
+    x = _rand_bf16(LENS, state=True, seed=15)
+    rule = GatedDeltaRule(algo="tensor_split", split_chunks=2)
+    o1, s1 = _gpu("chunked", x, rule)
+    assert _lib.load().gdr_release_scratch() == _lib.GDR_OK
+    o2, s2 = _gpu("chunked", x, rule)
+    assert (o1 == o2).all() and (s1 == s2).all()
