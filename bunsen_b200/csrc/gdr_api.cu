@@ -64,7 +64,8 @@ gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Pro
     const gdr_params& a = *params;
     if (a.heads_qk <= 0 || a.heads_v <= 0 || a.heads_v % a.heads_qk != 0) return GDR_ERR_INVALID;
     if (a.d_k <= 0 || a.d_v <= 0 || a.seq_len < 0) return GDR_ERR_INVALID;
-    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16) return GDR_ERR_INVALID;
+    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16 && a.dtype != GDR_DTYPE_F16)
+        return GDR_ERR_INVALID;
     if (a.use_l2norm && !(a.l2norm_eps >= 0.0)) return GDR_ERR_INVALID;
     if (cu_seqlens == nullptr && a.batch < 0) return GDR_ERR_INVALID;
     if (cu_seqlens != nullptr && a.n_seqs < 0) return GDR_ERR_INVALID;
@@ -94,11 +95,16 @@ bool io_ok(const Problem& p, const void* q, const void* k, const void* v, const 
 
 gdr_status from_cuda(cudaError_t e) { return e == cudaSuccess ? GDR_OK : GDR_ERR_CUDA; }
 
-enum class ChunkedPath { kNothing, kPassThrough, kTensor, kSplit, kCudaCore };
+enum class ChunkedPath { kNothing, kPassThrough, kTensor, kSplit, kCudaCore, kRecurrent };
+
+// The recurrent kernels' head sizes.
+constexpr int kRecurrentMaxD = 256;
 
 // Which kernels a gdr_chunked call runs: the checks of everything but the
 // buffers, then the algorithm (GDR_ALGO_AUTO: the tensor-core kernels where
-// they apply -- split into segments when that may help -- else the f32 one).
+// they apply -- split into segments when that may help -- else the f32
+// chunked kernel, else, for chunks above 64 or heads above 128, the recurrent
+// kernel: the same rule, delta_rule.rs:549-608).
 gdr_status chunked_path(const gdr_params* params, const int32_t* cu_seqlens, Problem& p,
                         ChunkedPath& path) {
     gdr_status st = make_problem(params, cu_seqlens, p);
@@ -111,17 +117,19 @@ gdr_status chunked_path(const gdr_params* params, const int32_t* cu_seqlens, Pro
     if (params->split_chunks < 0) return GDR_ERR_INVALID;
     const bool tc_ok = gdr::chunked_tc_supports(*params);
     const bool ffma_ok = gdr::chunked_ffma_supports(p.d_k, p.d_v, p.chunk);
+    const bool rec_ok = p.d_k <= kRecurrentMaxD && p.d_v <= kRecurrentMaxD;
     if (algo == GDR_ALGO_TENSOR || algo == GDR_ALGO_TENSOR_SPLIT) {
         if (!tc_ok) return GDR_ERR_UNSUPPORTED;
         path = algo == GDR_ALGO_TENSOR ? ChunkedPath::kTensor : ChunkedPath::kSplit;
     } else if (algo == GDR_ALGO_CUDA_CORE) {
-        if (!ffma_ok) return GDR_ERR_UNSUPPORTED;
-        path = ChunkedPath::kCudaCore;
+        if (!ffma_ok && !rec_ok) return GDR_ERR_UNSUPPORTED;
+        path = ffma_ok ? ChunkedPath::kCudaCore : ChunkedPath::kRecurrent;
     } else {
-        if (!tc_ok && !ffma_ok) return GDR_ERR_UNSUPPORTED;
-        path = !tc_ok ? ChunkedPath::kCudaCore
-               : (params->split_chunks > 0 || gdr::split_may_help(p)) ? ChunkedPath::kSplit
-                                                                       : ChunkedPath::kTensor;
+        if (!tc_ok && !ffma_ok && !rec_ok) return GDR_ERR_UNSUPPORTED;
+        path = tc_ok ? ((params->split_chunks > 0 || gdr::split_may_help(p)) ? ChunkedPath::kSplit
+                                                                             : ChunkedPath::kTensor)
+               : ffma_ok ? ChunkedPath::kCudaCore
+                         : ChunkedPath::kRecurrent;
     }
     if (p.n_seqs == 0) path = ChunkedPath::kNothing;
     else if (total_tokens(p) == 0) path = ChunkedPath::kPassThrough;
@@ -195,6 +203,7 @@ gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, c
         case ChunkedPath::kNothing:
             return GDR_OK;
         case ChunkedPath::kPassThrough:  // no tokens: the state passes through
+        case ChunkedPath::kRecurrent:
             return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in,
                                                    out, state_out, s));
         case ChunkedPath::kSplit:
@@ -256,7 +265,7 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
         max_tok = std::max<int64_t>(max_tok, first(cut[i + 1]) - first(cut[i]));
         max_seq = std::max<int64_t>(max_seq, cut[i + 1] - cut[i]);
     }
-    const size_t es = params->dtype == GDR_DTYPE_BF16 ? 2 : 4;
+    const size_t es = params->dtype == GDR_DTYPE_F32 ? 4 : 2;
     const size_t row_qk = static_cast<size_t>(p.heads_qk) * p.d_k * es;
     const size_t row_v = static_cast<size_t>(p.heads_v) * p.d_v * es;
     const size_t row_gb = static_cast<size_t>(p.heads_v) * sizeof(float);
@@ -369,7 +378,8 @@ gdr_status gdr_causal_conv1d(const gdr_conv_params* params, const void* x, const
     const int C = a.channels, K = a.taps;
     if (C <= 0 || K < 2 || a.seq_len < 0) return GDR_ERR_INVALID;  // causal_conv.rs:47
     if (K > gdr::conv_max_taps()) return GDR_ERR_UNSUPPORTED;
-    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16) return GDR_ERR_INVALID;
+    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16 && a.dtype != GDR_DTYPE_F16)
+        return GDR_ERR_INVALID;
     if (!(0 <= a.split0 && a.split0 <= a.split1 && a.split1 <= C)) return GDR_ERR_INVALID;
     const int32_t n = cu_seqlens ? a.n_seqs : a.batch;
     if (n < 0) return GDR_ERR_INVALID;
@@ -390,7 +400,8 @@ gdr_status gdr_gated_norm(int64_t rows, int32_t width, const void* x, const void
                           const float* weight, double eps, int32_t dtype, void* out,
                           void* stream) {
     if (rows < 0 || width <= 0 || !(eps >= 0.0)) return GDR_ERR_INVALID;
-    if (dtype != GDR_DTYPE_F32 && dtype != GDR_DTYPE_BF16) return GDR_ERR_INVALID;
+    if (dtype != GDR_DTYPE_F32 && dtype != GDR_DTYPE_BF16 && dtype != GDR_DTYPE_F16)
+        return GDR_ERR_INVALID;
     if (rows == 0) return GDR_OK;
     if (x == nullptr || z == nullptr || weight == nullptr || out == nullptr) return GDR_ERR_INVALID;
     return from_cuda(gdr::launch_gated_norm(dtype, rows, width, x, z, weight,
@@ -421,7 +432,8 @@ gdr_status check_layer_io(const gdr_layer_io& io, int64_t tokens, const float* g
                           const float* beta) {
     if (io.gate_a != nullptr) {
         if (g != nullptr || beta != nullptr) return GDR_ERR_INVALID;
-        if (io.gate_dtype != GDR_DTYPE_F32 && io.gate_dtype != GDR_DTYPE_BF16)
+        if (io.gate_dtype != GDR_DTYPE_F32 && io.gate_dtype != GDR_DTYPE_BF16 &&
+            io.gate_dtype != GDR_DTYPE_F16)
             return GDR_ERR_INVALID;
         if (tokens > 0 && (io.gate_b == nullptr || io.a_log == nullptr || io.dt_bias == nullptr))
             return GDR_ERR_INVALID;
@@ -438,6 +450,7 @@ void set_layer_gates(const gdr_layer_io& io, Problem& p) {
     p.gate_b = io.gate_b;
     p.a_log = io.a_log;
     p.dt_bias = io.dt_bias;
+    p.gate_dtype = io.gate_dtype;
     p.gate_bf16 = io.gate_dtype == GDR_DTYPE_BF16;
 }
 void set_layer_norm(const gdr_layer_io& io, Problem& p) {
@@ -473,9 +486,12 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
     if (!chunked && (p.d_k > 256 || p.d_v > 256)) return GDR_ERR_UNSUPPORTED;
     if (p.n_seqs == 0 || (chunked && path == ChunkedPath::kNothing)) return GDR_OK;
     const bool tc = chunked && (path == ChunkedPath::kTensor || path == ChunkedPath::kSplit);
+    const bool rec = !chunked || path == ChunkedPath::kRecurrent;  // the recurrent kernels
     const bool d128 = p.d_k == 128 && p.d_v == 128;
-    const bool fuse_gates = gates && (tc || !chunked);
-    const bool fuse_norm = norm && (tc || (!chunked && d128));
+    // The tensor-core prefill stages f32 or bf16 projections; the recurrent
+    // kernels read any gate dtype.
+    const bool fuse_gates = gates && ((tc && io->gate_dtype != GDR_DTYPE_F16) || rec);
+    const bool fuse_norm = norm && (tc || (rec && d128));
     // The tensor-core prefill stages 4-byte words of the projections and
     // reads z 16 bytes at a time.
     if (tc && fuse_gates &&
@@ -501,7 +517,7 @@ gdr_status layer_call(bool chunked, const gdr_params* params, const void* q, con
     }
     if (st == GDR_OK) {
         cudaError_t e;
-        if (!chunked || path == ChunkedPath::kPassThrough)
+        if (rec || path == ChunkedPath::kPassThrough)
             e = gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out, state_out,
                                       s);
         else if (path == ChunkedPath::kSplit)

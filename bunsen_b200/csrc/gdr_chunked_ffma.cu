@@ -260,6 +260,8 @@ cudaError_t launch_chunked_ffma(const Problem& p, int dtype, const void* q, cons
     if (dtype == GDR_DTYPE_BF16)
         return launch_ffma_t<__nv_bfloat16>(p, q, k, v, g, beta, state_in, out, state_out,
                                             stream);
+    if (dtype == GDR_DTYPE_F16)
+        return launch_ffma_t<__half>(p, q, k, v, g, beta, state_in, out, state_out, stream);
     return launch_ffma_t<float>(p, q, k, v, g, beta, state_in, out, state_out, stream);
 }
 

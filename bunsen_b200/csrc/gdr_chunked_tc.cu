@@ -429,7 +429,7 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
             x = __uint_as_float((__float_as_uint(x) >> ((i & 1) ? 16 : 0)) << 16);
         }
         ms.gstage[which][t] = pos >= len ? 0.f
-                              : which   ? gate_beta(x, p.gate_bf16)
+                              : which   ? gate_beta(x, p.gate_dtype)
                                         : gate_g(x, p.a_log[h], p.dt_bias[h]);
     };
     // Warp 0: the staged gates into the chunk's arrays, the log decay as its

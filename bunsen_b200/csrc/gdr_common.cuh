@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -28,7 +29,8 @@ struct Problem {
     const void* gate_b = nullptr;
     const float* a_log = nullptr;
     const float* dt_bias = nullptr;
-    int32_t gate_bf16 = 0;
+    int32_t gate_dtype = GDR_DTYPE_F32;  // gdr_dtype of a and b
+    int32_t gate_bf16 = 0;               // gate_dtype == GDR_DTYPE_BF16
     const void* norm_z = nullptr;
     const float* norm_w = nullptr;
     float norm_eps = 0.f;
@@ -52,6 +54,7 @@ __device__ __forceinline__ void seq_span(const Problem& p, int s, int64_t& start
 
 __device__ __forceinline__ float to_f32(float x) { return x; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
 
 template <typename T>
 __device__ __forceinline__ T from_f32(float x);
@@ -60,6 +63,10 @@ __device__ __forceinline__ float from_f32<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
     return __float2bfloat16_rn(x);
+}
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) {
+    return __float2half_rn(x);
 }
 
 __device__ __forceinline__ float warp_sum(float x) {
@@ -84,14 +91,17 @@ __device__ __forceinline__ float gate_g(float a, float a_log, float dt_bias) {
     const float sp = x > 20.f ? x : log1pf(expf(x));
     return -expf(a_log) * sp;
 }
-__device__ __forceinline__ float gate_beta(float b, int32_t bf16) {
+__device__ __forceinline__ float gate_beta(float b, int32_t dtype) {
     const float s = 1.f / (1.f + expf(-b));
-    return bf16 ? __bfloat162float(__float2bfloat16_rn(s)) : s;
+    return dtype == GDR_DTYPE_BF16  ? __bfloat162float(__float2bfloat16_rn(s))
+           : dtype == GDR_DTYPE_F16 ? __half2float(__float2half_rn(s))
+                                    : s;
 }
 
-__device__ __forceinline__ float load_gate_input(const void* base, int64_t i, int32_t bf16) {
-    return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
-                : static_cast<const float*>(base)[i];
+__device__ __forceinline__ float load_gate_input(const void* base, int64_t i, int32_t dtype) {
+    return dtype == GDR_DTYPE_BF16  ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i])
+           : dtype == GDR_DTYPE_F16 ? __half2float(static_cast<const __half*>(base)[i])
+                                    : static_cast<const float*>(base)[i];
 }
 
 // g and beta of position-and-head index i = t * H_v + h: from the call's
@@ -99,8 +109,8 @@ __device__ __forceinline__ float load_gate_input(const void* base, int64_t i, in
 __device__ __forceinline__ void rule_gates(const Problem& p, const float* g, const float* beta,
                                            int64_t i, int h, float& gi, float& bi) {
     if (p.gate_a != nullptr) {
-        gi = gate_g(load_gate_input(p.gate_a, i, p.gate_bf16), p.a_log[h], p.dt_bias[h]);
-        bi = gate_beta(load_gate_input(p.gate_b, i, p.gate_bf16), p.gate_bf16);
+        gi = gate_g(load_gate_input(p.gate_a, i, p.gate_dtype), p.a_log[h], p.dt_bias[h]);
+        bi = gate_beta(load_gate_input(p.gate_b, i, p.gate_dtype), p.gate_dtype);
     } else {
         gi = g[i];
         bi = beta[i];

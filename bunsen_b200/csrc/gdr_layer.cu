@@ -143,6 +143,10 @@ template <>
 __device__ __forceinline__ float2 load2<__nv_bfloat16>(const __nv_bfloat16* p) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
+template <>
+__device__ __forceinline__ float2 load2<__half>(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
 template <typename T>
 __device__ __forceinline__ void store2(T* p, float a, float b);
 template <>
@@ -152,6 +156,10 @@ __device__ __forceinline__ void store2<float>(float* p, float a, float b) {
 template <>
 __device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* p, float a, float b) {
     *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+template <>
+__device__ __forceinline__ void store2<__half>(__half* p, float a, float b) {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(a, b);
 }
 
 template <typename T, int K>
@@ -398,7 +406,9 @@ __global__ void gates_kernel(int64_t n, int heads, const T* __restrict__ a,
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int h = static_cast<int>(i % heads);
         g[i] = gate_g(to_f32(a[i]), a_log[h], dt_bias[h]);
-        beta[i] = gate_beta(to_f32(b[i]), sizeof(T) == 2);
+        beta[i] = gate_beta(to_f32(b[i]), std::is_same<T, __nv_bfloat16>::value ? GDR_DTYPE_BF16
+                                          : std::is_same<T, __half>::value      ? GDR_DTYPE_F16
+                                                                                 : GDR_DTYPE_F32);
     }
 }
 
@@ -555,10 +565,12 @@ cudaError_t launch_causal_conv1d(int dtype, int32_t n_seqs, int64_t tokens, int3
                                  const void* weight, const float* state_in, void* out0,
                                  void* out1, void* out2, float* state_out, cudaStream_t s) {
     const Conv p{n_seqs, tokens, seq_len, cu_seqlens, channels, taps, split0, split1, silu};
-    return dtype == GDR_DTYPE_BF16
-               ? launch_conv_t<__nv_bfloat16>(p, x, weight, state_in, out0, out1, out2,
-                                              state_out, s)
-               : launch_conv_t<float>(p, x, weight, state_in, out0, out1, out2, state_out, s);
+    if (dtype == GDR_DTYPE_BF16)
+        return launch_conv_t<__nv_bfloat16>(p, x, weight, state_in, out0, out1, out2, state_out,
+                                            s);
+    if (dtype == GDR_DTYPE_F16)
+        return launch_conv_t<__half>(p, x, weight, state_in, out0, out1, out2, state_out, s);
+    return launch_conv_t<float>(p, x, weight, state_in, out0, out1, out2, state_out, s);
 }
 
 cudaError_t launch_gates(int dtype, int64_t n, int heads, const void* a, const void* b,
@@ -569,6 +581,10 @@ cudaError_t launch_gates(int dtype, int64_t n, int heads, const void* a, const v
         gates_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, s>>>(
             n, heads, static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
             a_log, dt_bias, g, beta);
+    else if (dtype == GDR_DTYPE_F16)
+        gates_kernel<__half><<<grid_for(n, 256), 256, 0, s>>>(
+            n, heads, static_cast<const __half*>(a), static_cast<const __half*>(b), a_log,
+            dt_bias, g, beta);
     else
         gates_kernel<float><<<grid_for(n, 256), 256, 0, s>>>(
             n, heads, static_cast<const float*>(a), static_cast<const float*>(b), a_log, dt_bias,
@@ -593,6 +609,10 @@ cudaError_t launch_gated_norm(int dtype, int64_t rows, int width, const void* x,
         gated_norm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
             rows, width, static_cast<const __nv_bfloat16*>(x),
             static_cast<const __nv_bfloat16*>(z), weight, eps, static_cast<__nv_bfloat16*>(out));
+    else if (dtype == GDR_DTYPE_F16)
+        gated_norm_kernel<__half><<<grid, 256, 0, s>>>(
+            rows, width, static_cast<const __half*>(x), static_cast<const __half*>(z), weight, eps,
+            static_cast<__half*>(out));
     else
         gated_norm_kernel<float><<<grid, 256, 0, s>>>(rows, width, static_cast<const float*>(x),
                                                       static_cast<const float*>(z), weight, eps,

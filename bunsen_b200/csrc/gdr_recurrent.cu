@@ -132,6 +132,8 @@ cudaError_t launch_recurrent(const Problem& p, int dtype, const void* q, const v
     if (dtype == GDR_DTYPE_BF16)
         return launch_recurrent_t<__nv_bfloat16>(p, q, k, v, g, beta, state_in, out, state_out,
                                                  stream);
+    if (dtype == GDR_DTYPE_F16)
+        return launch_recurrent_t<__half>(p, q, k, v, g, beta, state_in, out, state_out, stream);
     return launch_recurrent_t<float>(p, q, k, v, g, beta, state_in, out, state_out, stream);
 }
 

@@ -35,7 +35,7 @@ def causal_conv1d(x, weight, state=None, *, cu_seqlens=None, silu=False, splits=
     if x.device.type != "cuda":
         raise RuntimeError("libgdr runs on CUDA tensors only")
     if x.dtype not in _DTYPES or weight.dtype != x.dtype:
-        raise TypeError("x and weight share one dtype, f32 or bf16")
+        raise TypeError("x and weight share one dtype, f32, bf16 or f16")
     packed = cu_seqlens is not None
     if x.dim() != (2 if packed else 3):
         raise ValueError("x is [B, T, C], or [T_total, C] with cu_seqlens")
@@ -75,7 +75,7 @@ def gated_norm(x, z, weight, eps, out=None):
     if x.device.type != "cuda":
         raise RuntimeError("libgdr runs on CUDA tensors only")
     if x.dtype not in _DTYPES or z.dtype != x.dtype or z.shape != x.shape:
-        raise TypeError("x and z share one shape and one dtype, f32 or bf16")
+        raise TypeError("x and z share one shape and one dtype, f32, bf16 or f16")
     x, z = x.contiguous(), z.contiguous()
     weight = weight.to(torch.float32).contiguous()
     if out is None:

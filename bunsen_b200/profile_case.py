@@ -6,6 +6,7 @@ cases the committed ncu summaries under profiles/ are captured on.
     python -m bunsen_b200.profile_case ragged_prefill --shard 8 --algo tensor_split
     python -m bunsen_b200.profile_case conv --scale 0.25         # the layer's conv
     python -m bunsen_b200.profile_case layer_prefill --scale 0.25  # gates + norm fused
+    python -m bunsen_b200.profile_case dense_prefill --dtype f32  # the f32 chunked kernel
 
 Prints the mean CUDA-event time per call. `--shard N` keeps the heads one GPU
 of an N-way head shard holds (H_qk / N key heads with their value heads).
@@ -36,11 +37,15 @@ def main() -> None:
                     choices=["auto", "tensor", "tensor_split", "cuda_core"])
     ap.add_argument("--split-chunks", type=int, default=0)
     ap.add_argument("--shard", type=int, default=1)
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16", "f32"],
+                    help="dtype of q, k, v and out (the workloads are bf16)")
     args = ap.parse_args()
     base = {"conv": "ragged_prefill", "layer_prefill": "ragged_prefill"}.get(args.workload,
                                                                              args.workload)
     w = workloads.get(base, scale=args.scale)
     x = workloads.make_inputs(w, "cuda", seed=1)
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[args.dtype]
+    x = {k: (v.to(dt) if k in ("q", "k", "v") else v) for k, v in x.items()}
     if args.shard > 1:
         hq, hv = w.heads_qk // args.shard, w.heads_v // args.shard
         heads = {"q": hq, "k": hq, "v": hv, "g": hv, "beta": hv}
@@ -87,7 +92,7 @@ def main() -> None:
         run()
     e1.record()
     e1.synchronize()
-    print(f"{args.workload} scale {args.scale} shard {args.shard} {args.algo}: "
+    print(f"{args.workload} scale {args.scale} shard {args.shard} {args.algo} {args.dtype}: "
           f"{e0.elapsed_time(e1) / args.iters:.4f} ms per call, "
           f"{w.tokens} tokens, {w.n_seqs} sequences")
 

@@ -24,7 +24,8 @@ import torch
 
 from . import _lib
 
-_DTYPES = {torch.float32: _lib.GDR_DTYPE_F32, torch.bfloat16: _lib.GDR_DTYPE_BF16}
+_DTYPES = {torch.float32: _lib.GDR_DTYPE_F32, torch.bfloat16: _lib.GDR_DTYPE_BF16,
+           torch.float16: _lib.GDR_DTYPE_F16}
 _ALGOS = {"auto": _lib.GDR_ALGO_AUTO, "cuda_core": _lib.GDR_ALGO_CUDA_CORE,
           "tensor": _lib.GDR_ALGO_TENSOR, "tensor_split": _lib.GDR_ALGO_TENSOR_SPLIT}
 
@@ -47,7 +48,7 @@ def _layer_io(gates, norm, q, v, g, beta):
             raise ValueError("with gates=(a, b, a_log, dt_bias), g and beta are None")
         a, b, a_log, dt_bias = gates
         if a.dtype not in _DTYPES or b.dtype != a.dtype:
-            raise TypeError("the gate projections a, b share one dtype, f32 or bf16")
+            raise TypeError("the gate projections a, b share one dtype, f32, bf16 or f16")
         a, b = a.contiguous(), b.contiguous()
         a_log = a_log.to(torch.float32).contiguous()
         dt_bias = dt_bias.to(torch.float32).contiguous()
@@ -168,7 +169,7 @@ class GatedDeltaRule:
         lead = 1 if packed else 2
         check_shapes(q, k, v, g, beta, state, cu_seqlens)
         if q.dtype not in _DTYPES:
-            raise TypeError(f"q, k, v in f32 or bf16, not {q.dtype}")
+            raise TypeError(f"q, k, v in f32, bf16 or f16, not {q.dtype}")
         if q.device.type != "cpu":
             raise RuntimeError("chunked_host takes host tensors; use chunked for CUDA tensors")
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else \
@@ -233,7 +234,7 @@ class GatedDeltaRule:
             io, keep, g, beta = _layer_io(gates, norm, q, v, g, beta)
         check_shapes(q, k, v, g, beta, state, cu_seqlens)
         if q.dtype not in _DTYPES:
-            raise TypeError(f"q, k, v in f32 or bf16, not {q.dtype}")
+            raise TypeError(f"q, k, v in f32, bf16 or f16, not {q.dtype}")
         dev = q.device
         if dev.type != "cuda":
             raise RuntimeError("libgdr runs on CUDA tensors only")

@@ -74,18 +74,29 @@ typedef enum gdr_status {
     GDR_ERR_CAPACITY = 5     /* more than a fixed-size entry point can take  */
 } gdr_status;
 
+/* q, k, v and out share one dtype. bunsen widens half-precision inputs to f32
+ * (burner/tensor/widening.rs:58-60) and narrows the output back: bf16 runs
+ * take bf16 operands on the tensor cores with f32 accumulation; f16 runs
+ * compute in f32 on the CUDA-core kernels, as f32 runs do. f64, which bunsen
+ * keeps as its compute dtype, is not served. */
 typedef enum gdr_dtype {
     GDR_DTYPE_F32 = 0,
-    GDR_DTYPE_BF16 = 1
+    GDR_DTYPE_BF16 = 1,
+    GDR_DTYPE_F16 = 2
 } gdr_dtype;
 
 /* Which kernel family runs a chunked call. AUTO picks the tensor-core kernels
  * for bf16, d_k = d_v = 128, chunk 64 -- split into segments when some
  * sequence could be longer than twice the smallest segment worth running
- * (see GDR_ALGO_TENSOR_SPLIT) -- and the CUDA-core f32 kernel otherwise. */
+ * (see GDR_ALGO_TENSOR_SPLIT) -- and the CUDA-core f32 kernel otherwise.
+ * Shapes that kernel does not take (chunk above 64, or d_k or d_v above 128,
+ * up to 256) run on the recurrent kernel, under AUTO and CUDA_CORE alike:
+ * bunsen's chunked and recurrent forms are the same rule and agree to f32
+ * rounding (delta_rule.rs:549-608), the chunk size only changing how. */
 typedef enum gdr_algo {
     GDR_ALGO_AUTO = 0,
-    GDR_ALGO_CUDA_CORE = 1,   /* f32 FFMA throughout: f32 runs, any small dims */
+    GDR_ALGO_CUDA_CORE = 1,   /* f32 FFMA throughout: f32 and f16 runs, any dims
+                                 up to 256                                    */
     GDR_ALGO_TENSOR = 2,      /* tcgen05/TMEM, bf16 operands, f32 accumulate;
                                  one pass per (sequence, head)                 */
     GDR_ALGO_TENSOR_SPLIT = 3 /* the same kernel over segments of the long

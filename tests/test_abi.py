@@ -131,6 +131,34 @@ def test_chunked_launch_counts():
     assert n(_params(algo=9)) == -1
 
 
+def test_dtype_and_shape_routes():
+    """f16 runs and the shapes the f32 chunked kernel does not take still
+    have a kernel: f16 computes in f32 on the CUDA cores (bunsen widens half
+    types to f32), a chunk above 64 or heads up to 256 run the recurrent
+    kernel (the same rule); only the tensor-core algorithms refuse them, and
+    heads above 256 have no kernel."""
+    lib = _lib.load()
+    n = lambda p, packed=1: lib.gdr_chunked_launches(ctypes.byref(p), packed)  # noqa: E731
+    tc = dict(d_k=128, d_v=128, chunk_size=64, n_seqs=4, seq_len=256)
+    f16 = dict(tc, dtype=_lib.GDR_DTYPE_F16)
+    assert n(_params(**f16)) == 1
+    assert n(_params(**f16, algo=_lib.GDR_ALGO_CUDA_CORE)) == 1
+    assert n(_params(**f16, algo=_lib.GDR_ALGO_TENSOR)) == -1
+    assert n(_params(**dict(tc, dtype=_lib.GDR_DTYPE_BF16, chunk_size=128))) == 1
+    assert n(_params(**dict(tc, dtype=_lib.GDR_DTYPE_BF16, chunk_size=128),
+                     algo=_lib.GDR_ALGO_TENSOR)) == -1
+    assert n(_params(**dict(tc, d_k=192, d_v=256))) == 1
+    assert n(_params(**dict(tc, d_k=192, d_v=256), algo=_lib.GDR_ALGO_CUDA_CORE)) == 1
+    assert n(_params(**dict(tc, d_k=257))) == -1
+    d = ctypes.c_void_p(16)
+    # gdr_mixed is tensor-core only: an f16 batch is refused before any launch.
+    p = _params(**dict(f16, n_seqs=1, seq_len=4))
+    cu = ctypes.c_void_p(16)
+    ws = ctypes.c_void_p(16)
+    assert lib.gdr_mixed(ctypes.byref(p), d, d, d, d, d, d, None, 1, d, cu, ws, 1 << 20,
+                         None) == _lib.GDR_ERR_UNSUPPORTED
+
+
 def test_host_call_rejects_malformed_offsets_before_any_copy():
     """gdr_chunked_host reads cu_seqlens on the host: offsets that do not start
     at 0, decrease, or miss T_total are GDR_ERR_INVALID before any CUDA call."""
