@@ -7,6 +7,7 @@ lognormal sequences, 16 q/k heads, 32 v heads, d 128, chunk 64, bf16, f32
 initial states), inputs resident in HBM (2.3 GB, larger than L2, so no flush
 is needed). Sub-objects carry the other workloads at the same N:
   dense    8 x 4096 tokens, zero initial state (gdr_chunked)
+  dense_f32  the same with f32 q, k, v (the f32 CUDA-core chunked kernel)
   decode   64 consecutive single-token steps over 256 rows, f32 states
            [256, 32, 128, 128] updated in place (gdr_recurrent)
   mixed    8 prefill segments x 2048 tokens + 1024 decode rows in one
@@ -393,6 +394,30 @@ def bench_prefill(name: str, args, dist, dev, stream, pk, pk_kind, e2e=False, ve
     return res
 
 
+def bench_dense_f32(args, dist, dev, stream, pk, pk_kind) -> dict:
+    """The dense configuration with f32 q, k, v (bunsen's f32 models): the f32
+    CUDA-core chunked kernel, every product an f32 FMA."""
+    w = workloads.get("dense_prefill")
+    sh = shard_of(w, dist)
+    x = sh.take(workloads.make_inputs(w, dev, seed=1234))
+    x = {k: (v.float() if k in ("q", "k", "v") else v) for k, v in x.items()}
+    hv = sh.v.stop - sh.v.start
+    rule = GatedDeltaRule(chunk_size=w.chunk)
+    out = torch.empty(x["v"].shape, dtype=torch.float32, device=dev)
+    st_out = torch.empty(w.n_seqs, hv, w.d_k, w.d_v, dtype=torch.float32, device=dev)
+
+    def step():
+        rule.chunked(x["q"], x["k"], x["v"], x["g"], x["beta"], None, out=out, state_out=st_out)
+
+    k = max(1, min(args.steps, 5))
+    total, per = timed(step, k, 1, dist, stream)
+    ms = total / k
+    return {"value": w.tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "dtype": "f32", "kernel": "chunked_ffma (f32 FMA)",
+            "gpu_launches": k * rule.chunked_launches(x["q"], x["v"]),
+            "tflops": prefill_flops(w, hv) / (statistics.mean(per) * 1e-3) / 1e12}
+
+
 def bench_e2e(w, x, rule, out, st_out, args, dist, dev, stream) -> dict:
     """The same rule through the public host-buffer call (``gdr_chunked_host``):
     each step copies every input from pinned host memory to the GPU, runs, and
@@ -599,6 +624,7 @@ def run_native(args, dist: Dist) -> None:
     rag = bench_prefill("ragged_prefill", args, dist, dev, stream, pk, pk_kind, e2e=True,
                         verify=args.verify)
     dense = bench_prefill("dense_prefill", args, dist, dev, stream, pk, pk_kind)
+    dense_f32 = bench_dense_f32(args, dist, dev, stream, pk, pk_kind)
     decode = bench_decode(args, dist, dev, stream, pk, pk_kind)
     mixed = bench_mixed(args, dist, dev, stream, pk, pk_kind)
     layer = bench_layer(args, dist, dev, stream, pk, pk_kind)
@@ -611,6 +637,7 @@ def run_native(args, dist: Dist) -> None:
         w = workloads.get("ragged_prefill")
         dense = {k: dense[k] for k in ("value", "unit", "ms_per_step", "roofline", "clocks")}
         dense["cpu_baseline"] = cpu.get("dense_prefill")
+        dense_f32["cpu_baseline"] = cpu.get("dense_prefill")  # the oracle runs in f32
         decode["cpu_baseline"] = cpu.get("decode")
         mixed["cpu_baseline"] = cpu.get("mixed")
         line = {"metric": METRIC, "value": rag["value"], "unit": "tokens/s",
@@ -620,7 +647,8 @@ def run_native(args, dist: Dist) -> None:
                 "config": headline_config(w, dist.world),
                 "roofline": rag["roofline"], "cpu_baseline": cpu.get("ragged_prefill"),
                 "e2e": rag["e2e"], "gpu_launches": rag["gpu_launches"], "clocks": rag["clocks"],
-                "dense": dense, "decode": decode, "mixed": mixed, "layer": layer}
+                "dense": dense, "dense_f32": dense_f32, "decode": decode, "mixed": mixed,
+                "layer": layer}
         if "verified" in rag:
             line["verified"] = rag["verified"]
         print(json.dumps(line), flush=True)

@@ -831,11 +831,11 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                         uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            const float y0 =
-                                x[2 * j] * r * wv[2 * j] * silu_bf16(__bfloat162float(zb[2 * j]));
-                            const float y1 = x[2 * j + 1] * r * wv[2 * j + 1] *
-                                             silu_bf16(__bfloat162float(zb[2 * j + 1]));
-                            yw[j] = pack_bf16(y0, y1);
+                            float s0 = __bfloat162float(zb[2 * j]);
+                            float s1 = __bfloat162float(zb[2 * j + 1]);
+                            silu2_bf16(s0, s1);
+                            yw[j] = pack_bf16(x[2 * j] * r * wv[2 * j] * s0,
+                                              x[2 * j + 1] * r * wv[2 * j + 1] * s1);
                         }
                         *reinterpret_cast<uint4*>(out + row) = y;
                     }

@@ -126,12 +126,34 @@ __device__ __forceinline__ float silu_f32(float x) { return __fdividef(x, 1.f + 
 // relative error is near 5e-3, the size of a bf16 step), so there the result
 // is x / (1 + e^-x) with the fast exponential instead (relative error below
 // 1e-5 until the result underflows to -0).
+// The exact form costs two more multi-function-unit instructions, so it runs
+// only in warps where some lane needs it (a vote over the lanes executing
+// together; each lane's own value always takes part in its vote).
 __device__ __forceinline__ float silu_bf16(float x) {
-    if (x < -3.f) return silu_f32(x);
     const float h = 0.5f * x;
     float t;
     asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
-    return fmaf(h, t, h);
+    float r = fmaf(h, t, h);
+    if (__any_sync(__activemask(), x < -3.f)) {
+        if (x < -3.f) r = silu_f32(x);
+    }
+    return r;
+}
+
+// silu_bf16 of two values with one vote.
+__device__ __forceinline__ void silu2_bf16(float& a, float& b) {
+    const float ha = 0.5f * a, hb = 0.5f * b;
+    float ta, tb;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(ta) : "f"(ha));
+    asm("tanh.approx.f32 %0, %1;" : "=f"(tb) : "f"(hb));
+    const float ra = fmaf(ha, ta, ha), rb = fmaf(hb, tb, hb);
+    if (__any_sync(__activemask(), fminf(a, b) < -3.f)) {
+        a = a < -3.f ? silu_f32(a) : ra;
+        b = b < -3.f ? silu_f32(b) : rb;
+    } else {
+        a = ra;
+        b = rb;
+    }
 }
 
 }  // namespace gdr

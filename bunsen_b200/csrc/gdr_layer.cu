@@ -350,10 +350,7 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
                 }
                 a0 = fmaf(xt.x, w0[K - 1], a0);
                 a1 = fmaf(xt.y, w1[K - 1], a1);
-                if (p.silu) {
-                    a0 = silu_bf16(a0);
-                    a1 = silu_bf16(a1);
-                }
+                if (p.silu) silu2_bf16(a0, a1);
                 *reinterpret_cast<__nv_bfloat162*>(out + t * stride + col) =
                     __floats2bfloat162_rn(a0, a1);
 #pragma unroll
