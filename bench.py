@@ -7,7 +7,7 @@ lognormal sequences, 16 q/k heads, 32 v heads, d 128, chunk 64, bf16, f32
 initial states), inputs resident in HBM (2.3 GB, larger than L2, so no flush
 is needed). Sub-objects carry the other workloads at the same N:
   dense    8 x 4096 tokens, zero initial state (gdr_chunked)
-  dense_f32  the same with f32 q, k, v (the f32 CUDA-core chunked kernel)
+  dense_f32  the same with f32 q, k, v (the register-tiled f32 CUDA-core kernel)
   decode   64 consecutive single-token steps over 256 rows, f32 states
            [256, 32, 128, 128] updated in place (gdr_recurrent)
   mixed    8 prefill segments x 2048 tokens + 1024 decode rows in one
@@ -395,8 +395,8 @@ def bench_prefill(name: str, args, dist, dev, stream, pk, pk_kind, e2e=False, ve
 
 
 def bench_dense_f32(args, dist, dev, stream, pk, pk_kind) -> dict:
-    """The dense configuration with f32 q, k, v (bunsen's f32 models): the f32
-    CUDA-core chunked kernel, every product an f32 FMA."""
+    """The dense configuration with f32 q, k, v (bunsen's f32 models): the
+    register-tiled f32 CUDA-core chunked kernel, every product an f32 FMA."""
     w = workloads.get("dense_prefill")
     sh = shard_of(w, dist)
     x = sh.take(workloads.make_inputs(w, dev, seed=1234))
@@ -413,7 +413,7 @@ def bench_dense_f32(args, dist, dev, stream, pk, pk_kind) -> dict:
     total, per = timed(step, k, 1, dist, stream)
     ms = total / k
     return {"value": w.tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
-            "dtype": "f32", "kernel": "chunked_ffma (f32 FMA)",
+            "dtype": "f32", "kernel": "chunked_f32_d128 (f32 FMA)",
             "gpu_launches": k * rule.chunked_launches(x["q"], x["v"]),
             "tflops": prefill_flops(w, hv) / (statistics.mean(per) * 1e-3) / 1e12}
 

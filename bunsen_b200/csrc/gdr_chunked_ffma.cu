@@ -253,10 +253,24 @@ static cudaError_t launch_ffma_t(const Problem& p, const void* q, const void* k,
     return cudaGetLastError();
 }
 
+bool chunked_f32_d128_supports(const Problem& p, int dtype, const void* q, const void* k,
+                               const void* v, const void* out, const float* state_in,
+                               const float* state_out);
+cudaError_t launch_chunked_f32_d128(const Problem& p, int dtype, const void* q, const void* k,
+                                    const void* v, const float* g, const float* beta,
+                                    const float* state_in, void* out, float* state_out,
+                                    cudaStream_t stream);
+
+// The CUDA-core chunked path: the register-tiled kernel for d_k = d_v = 128,
+// chunk 64 (gdr_chunked_f32.cu) when its vector accesses are aligned, this
+// kernel for every other shape.
 cudaError_t launch_chunked_ffma(const Problem& p, int dtype, const void* q, const void* k,
                                 const void* v, const float* g, const float* beta,
                                 const float* state_in, void* out, float* state_out,
                                 cudaStream_t stream) {
+    if (chunked_f32_d128_supports(p, dtype, q, k, v, out, state_in, state_out))
+        return launch_chunked_f32_d128(p, dtype, q, k, v, g, beta, state_in, out, state_out,
+                                       stream);
     if (dtype == GDR_DTYPE_BF16)
         return launch_ffma_t<__nv_bfloat16>(p, q, k, v, g, beta, state_in, out, state_out,
                                             stream);

@@ -166,3 +166,27 @@ def test_f16_layer_steps():
     y = gated_norm(torch.from_numpy(core).half().to(DEV), z, w, 1e-6)
     _ok()
     assert rel_err(_np(y), want) < TOL_F16_OUT
+
+
+@pytest.mark.parametrize("eps", [1e-6, None])
+@pytest.mark.parametrize("state", [False, True])
+@pytest.mark.parametrize("algo", ["auto", "cuda_core"])
+def test_f32_d128_chunked_against_oracle(eps, state, algo):
+    """f32 at the production head size: the register-tiled f32 kernel, every
+    padding case of a ragged pack, held to the oracle at 1e-4."""
+    lens = [70, 1, 64, 0, 130, 200, 63]
+    x = _inputs(lens, torch.float32, seed=8, state=state)
+    if eps is None:  # keep the rule stable without the norm: k of norm below 1
+        x["k"] = x["k"] * 0.9
+    o, s = _run("chunked", x, GatedDeltaRule(qk_l2norm_eps=eps, algo=algo))
+    wo, ws = _want("chunked", x, eps=eps)
+    assert rel_err(o, wo) < TOL_F32 and rel_err(s, ws) < TOL_F32, (rel_err(o, wo), rel_err(s, ws))
+
+
+def test_bf16_inputs_on_the_f32_kernel():
+    """bf16 inputs through GDR_ALGO_CUDA_CORE compute in f32: states to 1e-4,
+    outputs to their bf16 rounding."""
+    x = _inputs([300, 65], torch.bfloat16, seed=9)
+    o, s = _run("chunked", x, GatedDeltaRule(algo="cuda_core"))
+    wo, ws = _want("chunked", x)
+    assert rel_err(o, wo) < 1e-2 and rel_err(s, ws) < TOL_F32
