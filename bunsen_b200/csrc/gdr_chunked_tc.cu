@@ -1162,9 +1162,18 @@ mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             mbar_expect_tx(bar, kD * kD * 4);
             bulk_load(stage, it.st, kD * kD * 4, bar);
         };
+        // A row's first inputs (q, k, v, gates) load while the row before it
+        // is updated, as its state does.
+        auto row_in = [&](const MixedItem& it) {
+            int64_t a, b;
+            seq_span(p, it.s, a, b);
+            return decode_in(p, q, k, v, g, beta, a, it.h);
+        };
         uint32_t ph = 0;
         MixedItem cur = fetch(1);
         if (threadIdx.x == 0 && cur.s >= 0) stage_state(cur);
+        DecodeIn<__nv_bfloat16> cur_in{};
+        if (cur.s >= 0) cur_in = row_in(cur);
 #pragma unroll 1
         while (cur.s >= 0) {
             if (!mbar_wait(bar, ph, kWaitLimitNs)) atomicOr(&g_tc_error, 1);
@@ -1174,11 +1183,15 @@ mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
             fence_proxy_async();  // these reads, before the next bulk write
             const MixedItem next = fetch(1);  // (its barriers order the reads)
             if (threadIdx.x == 0 && next.s >= 0) stage_state(next);
+            DecodeIn<__nv_bfloat16> next_in;  // read only when there is a next row
+            if (next.s >= 0) next_in = row_in(next);
             int64_t t0, t1;
             seq_span(p, cur.s, t0, t1);
-            decode_positions<__nv_bfloat16>(p, q, k, v, g, beta, t0, t1, cur.h, st, out, smem);
+            decode_positions<__nv_bfloat16>(p, q, k, v, g, beta, t0, t1, cur.h, st, out, smem,
+                                            cur_in);
             decode_store_state(cur.st, st);
             cur = next;
+            cur_in = next_in;
         }
         __syncthreads();
         if (threadIdx.x == 0) mbar_inval(bar);

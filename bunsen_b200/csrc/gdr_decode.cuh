@@ -50,8 +50,75 @@ __device__ __forceinline__ void decode_store_state(float* dst, const DecodeState
             make_float4(st[r][0], st[r][1], st[r][2], st[r][3]);
 }
 
+// This thread's inputs of position t of value head h, as loaded (converted
+// where they are used, so that a load issued a position ahead is not waited
+// for at once): one element of q (threads 0-127) or k (128-255), and, for
+// threads 0-127, one of v and of the gated norm's z; g and beta, or, with the
+// layer's gates fused, the bits of the projections a and b.
+template <typename T>
+struct DecodeIn {
+    T qk, v, z;
+    uint32_t ga, gb;
+};
+
+__device__ __forceinline__ uint32_t gate_bits(const void* base, int64_t i, int32_t dtype) {
+    uint32_t x;
+    if (dtype == GDR_DTYPE_F32)
+        x = __float_as_uint(static_cast<const float*>(base)[i]);
+    else
+        x = static_cast<const uint16_t*>(base)[i];
+    return x;
+}
+
+__device__ __forceinline__ float gate_value(uint32_t x, int32_t dtype) {
+    return dtype == GDR_DTYPE_F32    ? __uint_as_float(x)
+           : dtype == GDR_DTYPE_BF16 ? __uint_as_float(x << 16)
+                                     : __half2float(__ushort_as_half(static_cast<unsigned short>(x)));
+}
+
+template <typename T>
+__device__ __forceinline__ DecodeIn<T> decode_in(const Problem& p, const T* __restrict__ q,
+                                                 const T* __restrict__ k,
+                                                 const T* __restrict__ v,
+                                                 const float* __restrict__ g,
+                                                 const float* __restrict__ beta, int64_t t,
+                                                 int h) {
+    const int tid = threadIdx.x;
+    DecodeIn<T> in;
+    const int64_t qk_off = (t * p.heads_qk + h / p.group) * kDecD;
+    in.qk = ((tid < 128) ? q : k)[qk_off + (tid & 127)];
+    const int64_t orow = (t * p.heads_v + h) * kDecD;
+    in.v = v[orow + (tid & 127)];
+    in.z = from_f32<T>(0.f);
+    if (p.norm_z != nullptr) in.z = static_cast<const T*>(p.norm_z)[orow + (tid & 127)];
+    const int64_t i = t * p.heads_v + h;
+    if (p.gate_a != nullptr) {
+        in.ga = gate_bits(p.gate_a, i, p.gate_dtype);
+        in.gb = gate_bits(p.gate_b, i, p.gate_dtype);
+    } else {
+        in.ga = __float_as_uint(g[i]);
+        in.gb = __float_as_uint(beta[i]);
+    }
+    return in;
+}
+
+// g and beta of a position from its loaded inputs (rule_gates' arithmetic).
+template <typename T>
+__device__ __forceinline__ void decode_gates(const Problem& p, const DecodeIn<T>& in, int h,
+                                             float& gt, float& bt) {
+    if (p.gate_a != nullptr) {
+        gt = gate_g(gate_value(in.ga, p.gate_dtype), p.a_log[h], p.dt_bias[h]);
+        bt = gate_beta(gate_value(in.gb, p.gate_dtype), p.gate_dtype);
+    } else {
+        gt = __uint_as_float(in.ga);
+        bt = __uint_as_float(in.gb);
+    }
+}
+
 // The rule over positions [t0, t1) of value head h, the state in registers.
-// `smem` holds a DecodeSmem.
+// `in0` holds position t0's inputs (decode_in); each position's loads for the
+// next one are issued before its own arithmetic, so no position waits for a
+// global round trip of its own. `smem` holds a DecodeSmem.
 template <typename T>
 __device__ __forceinline__ void decode_positions(const Problem& p, const T* __restrict__ q,
                                                  const T* __restrict__ k,
@@ -59,7 +126,8 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
                                                  const float* __restrict__ g,
                                                  const float* __restrict__ beta, int64_t t0,
                                                  int64_t t1, int h, DecodeState& st,
-                                                 T* __restrict__ out, uint8_t* smem) {
+                                                 T* __restrict__ out, uint8_t* smem,
+                                                 DecodeIn<T> in0) {
     constexpr int kD = kDecD, kWarps = kDecWarps, kRowsPerWarp = kDecRowsPerWarp;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     auto& sh = *reinterpret_cast<DecodeSmem*>(smem);
@@ -68,14 +136,16 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
     auto& delta_s = sh.delta_s;
     auto& scal = sh.scal;
     const int col = 4 * lane;
-    const int hq = h / p.group;
+    DecodeIn<T> in = in0;
     for (int64_t t = t0; t < t1; ++t) {
-        // q and k of this position, raw, into shared memory.
-        const int64_t qk_off = (t * p.heads_qk + hq) * kD;
-        qk_raw[tid >> 7][tid & 127] = to_f32(((tid < 128) ? q : k)[qk_off + (tid & 127)]);
-        const int64_t gate = t * p.heads_v + h;
+        // q and k of this position, raw, into shared memory; the next
+        // position's inputs on their way.
+        qk_raw[tid >> 7][tid & 127] = to_f32(in.qk);
+        const bool more = t + 1 < t1;
+        DecodeIn<T> nxt;
+        if (more) nxt = decode_in(p, q, k, v, g, beta, t + 1, h);
         float gt, bt;
-        rule_gates(p, g, beta, gate, h, gt, bt);
+        decode_gates(p, in, h, gt, bt);
         const float decay = __expf(gt);
         __syncthreads();
         if (warp < 3) {  // |q|^2, |k|^2, q.k
@@ -119,8 +189,7 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
                 read += red[0][w][tid];
                 qs += red[1][w][tid];
             }
-            const float vj = to_f32(v[orow + tid]);
-            const float d = (vj - read) * bt;
+            const float d = (to_f32(in.v) - read) * bt;
             delta_s[tid] = d;
             const float qk_dot = scal[3] * fq * fk;
             o = fmaf(d, qk_dot, qs);
@@ -135,8 +204,7 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
         __syncthreads();
         if (p.norm_z != nullptr && tid < kD) {  // gated RMS norm of the 128 outputs
             const float r = rsqrtf((sh.nrm[0] + sh.nrm[1] + sh.nrm[2] + sh.nrm[3]) / kD + p.norm_eps);
-            const float z = to_f32(static_cast<const T*>(p.norm_z)[orow + tid]);
-            out[orow + tid] = from_f32<T>(o * r * p.norm_w[tid] * silu_f32(z));
+            out[orow + tid] = from_f32<T>(o * r * p.norm_w[tid] * silu_f32(to_f32(in.z)));
         }
         float dl[4];
 #pragma unroll
@@ -148,6 +216,7 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
             for (int c = 0; c < 4; ++c) st[r][c] = fmaf(kr, dl[c], st[r][c]);
         }
         __syncthreads();  // qk_raw, red and delta_s are rewritten next position
+        if (more) in = nxt;
     }
 
 }
@@ -170,7 +239,9 @@ __device__ __forceinline__ void recurrent_d128_item(const Problem& p, const T* _
 #pragma unroll
         for (int r = 0; r < kDecRowsPerWarp; ++r) st[r][0] = st[r][1] = st[r][2] = st[r][3] = 0.f;
     }
-    decode_positions<T>(p, q, k, v, g, beta, t0, t1, h, st, out, smem);
+    DecodeIn<T> in0{};
+    if (t0 < t1) in0 = decode_in(p, q, k, v, g, beta, t0, h);
+    decode_positions<T>(p, q, k, v, g, beta, t0, t1, h, st, out, smem, in0);
     decode_store_state(state_out, st);
 }
 
