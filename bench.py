@@ -254,14 +254,19 @@ def cpu_runner(name: str, threads: int):
 
     w, f = cpu_inputs(name)
     args = lambda sl=slice(None): [f[k][sl] for k in ("q", "k", "v", "g", "beta")]  # noqa: E731
+    # Output buffers made once and reused by every run (as an allocator reuses
+    # them), so the runs time the rule, not first-touch page faults.
+    t, n = w.tokens, w.n_seqs
+    out = np.empty((t, w.heads_v, w.d_v), np.float32)
+    st = np.empty((n, w.heads_v, w.d_k, w.d_v), np.float32)
     if name in ("ragged_prefill", "dense_prefill"):
         def run():
             oracle.chunked(*args(), f.get("state"), cu_seqlens=f.get("cu_seqlens"),
-                           chunk_size=w.chunk, threads=threads)
+                           chunk_size=w.chunk, threads=threads, out=out, state_out=st)
         what = "f32 chunked oracle"
     elif name == "decode":
         def run():
-            oracle.recurrent(*args(), f["state"], threads=threads)
+            oracle.recurrent(*args(), f["state"], threads=threads, out=out, state_out=st)
         what = "f32 recurrent oracle, one step"
     elif name == "mixed":
         n_pre = sum(1 for L in w.seqlens if L > 1)
@@ -271,12 +276,13 @@ def cpu_runner(name: str, threads: int):
 
         def run():
             oracle.chunked(*pre, f["state"][:n_pre], cu_seqlens=cu, chunk_size=w.chunk,
-                           threads=threads)
-            oracle.recurrent(*dec, f["state"][n_pre:], threads=threads)
+                           threads=threads, out=out[:t_pre], state_out=st[:n_pre])
+            oracle.recurrent(*dec, f["state"][n_pre:], threads=threads, out=out[t_pre:],
+                             state_out=st[n_pre:])
         what = "f32 chunked oracle on the prefill segments + recurrent on the decode rows"
     else:
         raise KeyError(name)
-    return w, run, f"the whole {name} workload ({what}, {threads} threads)"
+    return w, run, f"the whole {name} workload ({what}, {threads} threads, outputs reused)"
 
 
 def time_cpu(run, seconds: float) -> tuple[float, int]:

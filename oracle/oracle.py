@@ -80,7 +80,8 @@ def _pack(q, k, v, g, beta, state, cu_seqlens):
     return [q, k, v, g, beta], np.ascontiguousarray(cu_seqlens, dtype=np.int32), None
 
 
-def _run(fn: str, dtype, q, k, v, g, beta, state, l2norm_eps, chunk_size, cu_seqlens, threads):
+def _run(fn: str, dtype, q, k, v, g, beta, state, l2norm_eps, chunk_size, cu_seqlens, threads,
+         out=None, state_out=None):
     (q, k, v, g, beta), cu, dense = _pack(q, k, v, g, beta, state, cu_seqlens)
     q, k, v, g, beta = (np.ascontiguousarray(x, dtype=dtype) for x in (q, k, v, g, beta))
     t_total, h_qk, d_k = q.shape
@@ -88,8 +89,16 @@ def _run(fn: str, dtype, q, k, v, g, beta, state, l2norm_eps, chunk_size, cu_seq
     n = len(cu) - 1
     assert k.shape == q.shape and v.shape[0] == t_total and g.shape == beta.shape == (t_total, h_v)
     assert int(cu[-1]) == t_total
-    out = np.zeros((t_total, h_v, d_v), dtype=dtype)
-    st_out = np.zeros((n, h_v, d_k, d_v), dtype=dtype)
+    # Output buffers may be the caller's (reused between timed runs, so that
+    # first-touch page faults of fresh buffers are not timed).
+    if out is None:
+        out = np.zeros((t_total, h_v, d_v), dtype=dtype)
+    if state_out is None:
+        state_out = np.zeros((n, h_v, d_k, d_v), dtype=dtype)
+    assert out.shape == (t_total, h_v, d_v) and out.dtype == dtype and out.flags.c_contiguous
+    assert state_out.shape == (n, h_v, d_k, d_v) and state_out.dtype == dtype
+    assert state_out.flags.c_contiguous
+    st_out = state_out
     st_in = None
     if state is not None:
         st_in = np.ascontiguousarray(state, dtype=dtype).reshape(n, h_v, d_k, d_v)
@@ -106,19 +115,22 @@ def _run(fn: str, dtype, q, k, v, g, beta, state, l2norm_eps, chunk_size, cu_seq
     return out, st_out
 
 
-def recurrent(q, k, v, g, beta, state=None, *, l2norm_eps=1e-6, cu_seqlens=None, threads=0):
-    """``GatedDeltaRule::recurrent`` in f32 (``delta_rule.rs:182-209``)."""
+def recurrent(q, k, v, g, beta, state=None, *, l2norm_eps=1e-6, cu_seqlens=None, threads=0,
+              out=None, state_out=None):
+    """``GatedDeltaRule::recurrent`` in f32 (``delta_rule.rs:182-209``);
+    ``out`` / ``state_out``: packed f32 buffers to write into."""
     return _run("gdr_oracle_recurrent", np.float32, q, k, v, g, beta, state, l2norm_eps, 1,
-                cu_seqlens, threads)
+                cu_seqlens, threads, out, state_out)
 
 
 def chunked(q, k, v, g, beta, state=None, *, chunk_size=64, l2norm_eps=1e-6, cu_seqlens=None,
-            threads=0):
-    """``GatedDeltaRule::chunked`` in f32 (``delta_rule.rs:223-310``)."""
+            threads=0, out=None, state_out=None):
+    """``GatedDeltaRule::chunked`` in f32 (``delta_rule.rs:223-310``);
+    ``out`` / ``state_out``: packed f32 buffers to write into."""
     if chunk_size <= 0:
         raise ValueError("a chunk of at least one position")
     return _run("gdr_oracle_chunked", np.float32, q, k, v, g, beta, state, l2norm_eps,
-                chunk_size, cu_seqlens, threads)
+                chunk_size, cu_seqlens, threads, out, state_out)
 
 
 def scalar_f64(q, k, v, g, beta, state=None, *, l2norm_eps=1e-6, cu_seqlens=None, threads=0):
