@@ -831,9 +831,8 @@ __device__ __forceinline__ void prefill_item(const Problem& p, const CUtensorMap
                         uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            float s0 = __bfloat162float(zb[2 * j]);
-                            float s1 = __bfloat162float(zb[2 * j + 1]);
-                            silu2_bf16(s0, s1);
+                            const float s0 = silu(__bfloat162float(zb[2 * j]));
+                            const float s1 = silu(__bfloat162float(zb[2 * j + 1]));
                             yw[j] = pack_bf16(x[2 * j] * r * wv[2 * j] * s0,
                                               x[2 * j + 1] * r * wv[2 * j + 1] * s1);
                         }

@@ -117,43 +117,16 @@ __device__ __forceinline__ void rule_gates(const Problem& p, const float* g, con
     }
 }
 
-// x sigmoid(x) with the fast exponential and divide (0 for very negative x).
-__device__ __forceinline__ float silu_f32(float x) { return __fdividef(x, 1.f + __expf(-x)); }
-
-// silu for bf16 results: x sigmoid(x) = h + h tanh(h), h = x / 2, with the
-// one-instruction tanh, whose error is about 2^-11 of tanh itself. Below
-// x = -3, 1 + tanh(h) loses digits to cancellation (at x = -3 the result's
-// relative error is near 5e-3, the size of a bf16 step), so there the result
-// is x / (1 + e^-x) with the fast exponential instead (relative error below
-// 1e-5 until the result underflows to -0).
-// The exact form costs two more multi-function-unit instructions, so it runs
-// only in warps where some lane needs it (a vote over the lanes executing
-// together; each lane's own value always takes part in its vote).
-__device__ __forceinline__ float silu_bf16(float x) {
-    const float h = 0.5f * x;
-    float t;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
-    float r = fmaf(h, t, h);
-    if (__any_sync(__activemask(), x < -3.f)) {
-        if (x < -3.f) r = silu_f32(x);
-    }
-    return r;
-}
-
-// silu_bf16 of two values with one vote.
-__device__ __forceinline__ void silu2_bf16(float& a, float& b) {
-    const float ha = 0.5f * a, hb = 0.5f * b;
-    float ta, tb;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(ta) : "f"(ha));
-    asm("tanh.approx.f32 %0, %1;" : "=f"(tb) : "f"(hb));
-    const float ra = fmaf(ha, ta, ha), rb = fmaf(hb, tb, hb);
-    if (__any_sync(__activemask(), fminf(a, b) < -3.f)) {
-        a = a < -3.f ? silu_f32(a) : ra;
-        b = b < -3.f ? silu_f32(b) : rb;
-    } else {
-        a = ra;
-        b = rb;
-    }
+// x sigmoid(x) = x / (1 + e^-x), written so neither side cancels: with
+// u = e^-|x| (ex2.approx) and r = 1 / (1 + u) (rcp.approx), sigmoid(x) is r
+// for x >= 0 and u r below. Relative error below 1e-6 for |x| < 10 and below
+// 4e-6 for |x| < 100 (the rounding of the exponent's argument); the result
+// underflows to -0 below x = -87.
+__device__ __forceinline__ float silu(float x) {
+    float u, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(u) : "f"(-1.44269504f * fabsf(x)));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + u));
+    return x * (x >= 0.f ? r : u * r);
 }
 
 }  // namespace gdr

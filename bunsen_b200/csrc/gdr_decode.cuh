@@ -204,7 +204,7 @@ __device__ __forceinline__ void decode_positions(const Problem& p, const T* __re
         __syncthreads();
         if (p.norm_z != nullptr && tid < kD) {  // gated RMS norm of the 128 outputs
             const float r = rsqrtf((sh.nrm[0] + sh.nrm[1] + sh.nrm[2] + sh.nrm[3]) / kD + p.norm_eps);
-            out[orow + tid] = from_f32<T>(o * r * p.norm_w[tid] * silu_f32(to_f32(in.z)));
+            out[orow + tid] = from_f32<T>(o * r * p.norm_w[tid] * silu(to_f32(in.z)));
         }
         float dl[4];
 #pragma unroll

@@ -25,8 +25,6 @@ cudaError_t take_layer_error(int* flag) {
 
 namespace {
 
-__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
-
 // ---- causal depthwise convolution (causal_conv.rs:36-69) -------------------
 struct Conv {
     int32_t n_seqs;
@@ -120,7 +118,7 @@ conv_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ weight,
 #pragma unroll
         for (int j = 1; j < K - 1; ++j) acc = fmaf(h[j], w[j], acc);
         acc = fmaf(xt, w[K - 1], acc);
-        if (p.silu) acc = silu_f(acc);
+        if (p.silu) acc = silu(acc);
         out[t * stride + col] = from_f32<T>(acc);
 #pragma unroll
         for (int i = 0; i + 1 < K - 1; ++i) h[i] = h[i + 1];
@@ -228,8 +226,8 @@ conv_vec_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ wei
                 a0 = fmaf(xr[r].x, w0[K - 1], a0);
                 a1 = fmaf(xr[r].y, w1[K - 1], a1);
                 if (p.silu) {
-                    a0 = silu_f(a0);
-                    a1 = silu_f(a1);
+                    a0 = silu(a0);
+                    a1 = silu(a1);
                 }
                 store2(out + t * stride + col, a0, a1);
 #pragma unroll
@@ -240,32 +238,36 @@ conv_vec_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ wei
     }
 }
 
-// bf16 with C a multiple of 8: a CTA walks kStageSpan positions of 256
-// channels (two per thread), the rows of each 16-position window staged into
-// shared memory by cp.async while the window before is computed, so the
-// loads stay in flight whatever the threads are doing (16 KiB per CTA; the
-// registers, not the staging, bound the CTAs per SM). On B200, 131 072
-// positions x 8192 channels run at 0.80 of the measured HBM copy rate (0.66
-// with silu by the exact exponential, 0.47 with the register-only kernel);
-// deeper staging and wider tiles were no faster.
-constexpr int kStageRows = 16, kStageCols = 256, kStageSpan = 512;
+// bf16 with C and the split points multiples of 8: a CTA walks kStageSpan
+// positions of 1024 channels (eight per thread, one 16-byte load and store per
+// position), the rows of each 16-position window staged into shared memory by
+// cp.async while the window before is computed, so the loads stay in flight
+// whatever the threads are doing (64 KiB per CTA). Positions run in stretches
+// between sequence starts, so the per-position loop carries no boundary test
+// and unrolls. The kernel is bound by instruction issue as much as by HBM: on
+// B200, 131 072 positions x 8192 channels with silu run at 0.88 of the measured
+// HBM copy rate this way (0.97 without silu; 0.57 with two channels per thread
+// and a boundary test per position).
+constexpr int kStageRows = 16, kStageCh = 8, kStageCols = kConvThreads * kStageCh,
+              kStageSpan = 512;
 constexpr uint32_t kStageBytes = 2u * kStageRows * kStageCols * 2;  // two windows
 
-template <int K>
-__global__ void __launch_bounds__(kConvThreads)
+template <int K, bool kSilu>
+__global__ void __launch_bounds__(kConvThreads, K <= 4 ? 4 : 2)
 conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
                    const __nv_bfloat16* __restrict__ weight, const float* state,
                    __nv_bfloat16* out0, __nv_bfloat16* out1, __nv_bfloat16* out2) {
+    constexpr int NP = kStageCh / 2;  // channel pairs per thread
     extern __shared__ __align__(16) uint8_t conv_smem[];
-    auto* buf = reinterpret_cast<__nv_bfloat16*>(conv_smem);  // [2][64][256]
+    auto* buf = reinterpret_cast<__nv_bfloat16*>(conv_smem);  // [2][16][1024]
     const int C = p.channels, tid = threadIdx.x;
     const int cb = blockIdx.x * kStageCols;
-    const int c0 = cb + 2 * tid;
+    const int c0 = cb + kStageCh * tid;
     const int64_t T0 = static_cast<int64_t>(blockIdx.y) * kStageSpan;
     if (T0 >= p.tokens) return;
     const int64_t T1 = T0 + kStageSpan < p.tokens ? T0 + kStageSpan : p.tokens;
     const int windows = static_cast<int>((T1 - T0 + kStageRows - 1) / kStageRows);
-    auto load_window = [&](int w) {  // kStageRows rows x 32 16-byte pieces
+    auto load_window = [&](int w) {  // kStageRows rows x 128 16-byte pieces
         __nv_bfloat16* dst = buf + (w & 1) * kStageRows * kStageCols;
 #pragma unroll 4
         for (int e = tid; e < kStageRows * (kStageCols / 8); e += kConvThreads) {
@@ -283,8 +285,8 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
     };
     load_window(0);
     const bool active = c0 < C;
-    float w0[K], w1[K];
-    float2 h[K - 1];
+    float2 w[NP][K];      // the taps of channel pair q
+    float2 h[NP][K - 1];  // the K - 1 inputs before the current position
     int s = 0;
     int64_t start = 0, end = 0;
     __nv_bfloat16* out = nullptr;
@@ -292,20 +294,24 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
     int col = 0;
     if (active) {
 #pragma unroll
-        for (int j = 0; j < K; ++j) {
-            w0[j] = to_f32(weight[static_cast<int64_t>(c0) * K + j]);
-            w1[j] = to_f32(weight[static_cast<int64_t>(c0 + 1) * K + j]);
-        }
+        for (int q = 0; q < NP; ++q)
+#pragma unroll
+            for (int j = 0; j < K; ++j)
+                w[q][j] = make_float2(to_f32(weight[static_cast<int64_t>(c0 + 2 * q) * K + j]),
+                                      to_f32(weight[static_cast<int64_t>(c0 + 2 * q + 1) * K + j]));
         s = conv_seq_of(p, T0);
         conv_span(p, s, start, end);
 #pragma unroll
         for (int i = 0; i < K - 1; ++i) {
             const int64_t u = T0 - (K - 1) + i;
-            h[i] = u >= start ? load2(x + u * C + c0)
-                   : (state && start - u <= K - 1)
-                       ? *reinterpret_cast<const float2*>(
-                             state + (static_cast<int64_t>(s) * (K - 1) + (K - 1) - (start - u)) * C + c0)
-                       : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < NP; ++q)
+                h[q][i] = u >= start ? load2(x + u * C + c0 + 2 * q)
+                          : (state && start - u <= K - 1)
+                              ? *reinterpret_cast<const float2*>(
+                                    state + (static_cast<int64_t>(s) * (K - 1) + (K - 1) - (start - u)) * C +
+                                    c0 + 2 * q)
+                              : make_float2(0.f, 0.f);
         }
         if (c0 < p.split0) {
             out = out0, stride = p.split0, col = c0;
@@ -316,49 +322,68 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
         }
     }
 #pragma unroll 1
-    for (int w = 0; w < windows; ++w) {
-        if (w + 1 < windows) {
-            load_window(w + 1);
+    for (int wi = 0; wi < windows; ++wi) {
+        if (wi + 1 < windows) {
+            load_window(wi + 1);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        __syncthreads();  // window w has landed for every thread
+        __syncthreads();  // window wi has landed for every thread
         if (active) {
-            const __nv_bfloat16* rows = buf + (w & 1) * kStageRows * kStageCols + 2 * tid;
-            const int64_t tw = T0 + static_cast<int64_t>(w) * kStageRows;
+            const __nv_bfloat16* rows = buf + (wi & 1) * kStageRows * kStageCols + kStageCh * tid;
+            const int64_t tw = T0 + static_cast<int64_t>(wi) * kStageRows;
             const int n = static_cast<int>(T1 - tw < kStageRows ? T1 - tw : kStageRows);
-#pragma unroll 4
-            for (int r = 0; r < n; ++r) {
-                const int64_t t = tw + r;
-                while (t >= end && s + 1 < p.n_seqs) {  // into the next sequence
+            int r = 0;
+            while (r < n) {
+                while (tw + r >= end && s + 1 < p.n_seqs) {  // into the next sequence
                     ++s;
                     conv_span(p, s, start, end);
 #pragma unroll
                     for (int i = 0; i < K - 1; ++i)
-                        h[i] = state ? *reinterpret_cast<const float2*>(
-                                           state + (static_cast<int64_t>(s) * (K - 1) + i) * C + c0)
-                                     : make_float2(0.f, 0.f);
-                }
-                const float2 xt =
-                    __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rows + r * kStageCols));
-                float a0 = h[0].x * w0[0], a1 = h[0].y * w1[0];
 #pragma unroll
-                for (int j = 1; j < K - 1; ++j) {
-                    a0 = fmaf(h[j].x, w0[j], a0);
-                    a1 = fmaf(h[j].y, w1[j], a1);
+                        for (int q = 0; q < NP; ++q)
+                            h[q][i] = state ? *reinterpret_cast<const float2*>(
+                                                  state + (static_cast<int64_t>(s) * (K - 1) + i) * C +
+                                                  c0 + 2 * q)
+                                            : make_float2(0.f, 0.f);
                 }
-                a0 = fmaf(xt.x, w0[K - 1], a0);
-                a1 = fmaf(xt.y, w1[K - 1], a1);
-                if (p.silu) silu2_bf16(a0, a1);
-                *reinterpret_cast<__nv_bfloat162*>(out + t * stride + col) =
-                    __floats2bfloat162_rn(a0, a1);
+                // Positions up to the next sequence start (the last sequence
+                // runs to the window's end).
+                const int stop = s + 1 < p.n_seqs && end - tw < n ? static_cast<int>(end - tw) : n;
+#pragma unroll 3  // K = 4: the K - 1 history registers rotate in place
+                for (; r < stop; ++r) {
+                    const uint4 xv = *reinterpret_cast<const uint4*>(rows + r * kStageCols);
+                    const uint32_t xw[NP] = {xv.x, xv.y, xv.z, xv.w};
+                    uint32_t y[NP];
 #pragma unroll
-                for (int i = 0; i + 1 < K - 1; ++i) h[i] = h[i + 1];
-                h[K - 2] = xt;
+                    for (int q = 0; q < NP; ++q) {
+                        const float2 xt =
+                            __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[q]));
+                        float a0 = h[q][0].x * w[q][0].x, a1 = h[q][0].y * w[q][0].y;
+#pragma unroll
+                        for (int j = 1; j < K - 1; ++j) {
+                            a0 = fmaf(h[q][j].x, w[q][j].x, a0);
+                            a1 = fmaf(h[q][j].y, w[q][j].y, a1);
+                        }
+                        a0 = fmaf(xt.x, w[q][K - 1].x, a0);
+                        a1 = fmaf(xt.y, w[q][K - 1].y, a1);
+                        if (kSilu) {
+                            a0 = silu(a0);
+                            a1 = silu(a1);
+                        }
+                        const __nv_bfloat162 yq = __floats2bfloat162_rn(a0, a1);
+                        y[q] = *reinterpret_cast<const uint32_t*>(&yq);
+#pragma unroll
+                        for (int i = 0; i + 1 < K - 1; ++i) h[q][i] = h[q][i + 1];
+                        h[q][K - 2] = xt;
+                    }
+                    *reinterpret_cast<uint4*>(out + (tw + r) * stride + col) =
+                        make_uint4(y[0], y[1], y[2], y[3]);
+                }
             }
         }
-        __syncthreads();  // window w's buffer is free for window w + 2
+        __syncthreads();  // window wi's buffer is free for window wi + 2
     }
 }
 
@@ -427,7 +452,7 @@ __global__ void gated_norm_kernel(int64_t rows, int width, const T* x, const T* 
     const float r = rsqrtf(ss / width + eps);
     for (int i = lane; i < width; i += 32) {
         const float v = to_f32(xr[i]) * r * weight[i];
-        out[row * width + i] = from_f32<T>(v * silu_f(to_f32(z[row * width + i])));
+        out[row * width + i] = from_f32<T>(v * silu(to_f32(z[row * width + i])));
     }
 }
 
@@ -460,9 +485,9 @@ gated_norm_bf16_128(int64_t rows, const __nv_bfloat16* x, const __nv_bfloat16* _
         if (r0 + r < rows) {
             uint2 y;
             *reinterpret_cast<__nv_bfloat162*>(&y.x) = __floats2bfloat162_rn(
-                a.x * rs * wv.x * silu_f(za.x), a.y * rs * wv.y * silu_f(za.y));
+                a.x * rs * wv.x * silu(za.x), a.y * rs * wv.y * silu(za.y));
             *reinterpret_cast<__nv_bfloat162*>(&y.y) = __floats2bfloat162_rn(
-                b.x * rs * wv.z * silu_f(zb.x), b.y * rs * wv.w * silu_f(zb.y));
+                b.x * rs * wv.z * silu(zb.x), b.y * rs * wv.w * silu(zb.y));
             reinterpret_cast<uint2*>(out + (r0 + r) * 128)[lane] = y;
         }
     }
@@ -502,12 +527,16 @@ void launch_conv_k(const Conv& p, const void* x, const void* w, const float* st,
                      (al & 7) == 0;
     const unsigned ty = static_cast<unsigned>((p.tokens + kConvTokens - 1) / kConvTokens);
     if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        if (vec && p.channels % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-            cudaFuncSetAttribute(conv_staged_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const uintptr_t al16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(o0) |
+                               reinterpret_cast<uintptr_t>(o1) | reinterpret_cast<uintptr_t>(o2);
+        if (vec && p.channels % kStageCh == 0 && p.split0 % kStageCh == 0 &&
+            p.split1 % kStageCh == 0 && (al16 & 15) == 0) {
+            auto* kern = p.silu ? conv_staged_kernel<K, true> : conv_staged_kernel<K, false>;
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kStageBytes));
             const dim3 grid((p.channels + kStageCols - 1) / kStageCols,
                             static_cast<unsigned>((p.tokens + kStageSpan - 1) / kStageSpan));
-            conv_staged_kernel<K><<<grid, kConvThreads, kStageBytes, s>>>(
+            kern<<<grid, kConvThreads, kStageBytes, s>>>(
                 p, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), st,
                 static_cast<__nv_bfloat16*>(o0), static_cast<__nv_bfloat16*>(o1),
                 static_cast<__nv_bfloat16*>(o2));
