@@ -446,6 +446,19 @@ def bench_e2e(w, x, rule, out, st_out, args, dist, dev, stream) -> dict:
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 
+L2_BYTES = 126 * 2**20  # B200
+
+
+def l2_note(state_bytes_per_rank: float) -> str:
+    """Whether a rank's share of a state pool updated in place step after
+    step can stay in L2 between steps (no flush is done)."""
+    mb = state_bytes_per_rank / 2**20
+    if state_bytes_per_rank > L2_BYTES:
+        return f"states {mb:.0f} MiB per rank, larger than L2 (126 MiB): streamed from HBM"
+    return (f"states {mb:.0f} MiB per rank fit in L2 (126 MiB): consecutive steps may "
+            "hit L2, as a decode loop of this size does")
+
+
 def bench_decode(args, dist, dev, stream, pk, pk_kind) -> dict:
     w = workloads.get("decode")
     sh = shard_of(w, dist)
@@ -490,7 +503,8 @@ def bench_decode(args, dist, dev, stream, pk, pk_kind) -> dict:
             "unit": "GB/s", "ms_per_step": ms, "steps_timed": k * steps_per, "cuda_graph": True,
             "gpu_launches": k * steps_per,
             "config": {"workload": "decode", "rows": w.n_seqs, "heads_qk": w.heads_qk,
-                       "heads_v": w.heads_v, "d": w.d_k, "state_bytes_rw": state_rw},
+                       "heads_v": w.heads_v, "d": w.d_k, "state_bytes_rw": state_rw,
+                       "l2": l2_note(state_rw / 2 / dist.world)},
             "roofline": {"bound": "hbm", "achieved": local_bytes / (kern_ms * 1e-3) / 1e9,
                          "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": local_bytes / (kern_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
