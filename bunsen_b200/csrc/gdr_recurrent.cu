@@ -15,8 +15,9 @@
 //    q^T S) run in one pass: o = q^T S_decayed + delta (q . k), which is
 //    q^T S after the rank-one update. One smem exchange per position.
 //  * recurrent_generic -- any d_k, d_v <= 256: the state in shared memory,
-//    one thread per column. For small or unusual head sizes (bunsen's unit
-//    test shapes); not a performance path.
+//    one thread per column, in column blocks of one CTA each when the state
+//    is large. For small or unusual head sizes (bunsen's unit test shapes);
+//    not a performance path.
 #include "gdr_common.cuh"
 #include "gdr_decode.cuh"
 
@@ -39,25 +40,31 @@ recurrent_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
                            out, state_out + hs, smem);
 }
 
-// Any d_k, d_v <= 256. Shared memory: the state (d_k * d_v f32), q and k.
+// Any d_k, d_v <= 256. A state's columns evolve independently (column j
+// needs only k, q and v[j]), so each CTA takes `cols` of them (grid z) and
+// keeps S[:, c0 .. c0 + w) in shared memory, with q and k.
 template <typename T>
 __global__ void __launch_bounds__(128)
 recurrent_generic(Problem p, const T* __restrict__ q, const T* __restrict__ k,
                   const T* __restrict__ v, const float* __restrict__ g,
                   const float* __restrict__ beta, const float* state_in, T* __restrict__ out,
-                  float* state_out) {
+                  float* state_out, int cols) {
     extern __shared__ float smem[];
     const int dk = p.d_k, dv = p.d_v;
-    float* S = smem;                 // [dk][dv]
-    float* qv = S + dk * dv;         // [dk]
+    const int c0 = static_cast<int>(blockIdx.z) * cols;
+    const int w = dv - c0 < cols ? dv - c0 : cols;  // this CTA's columns
+    float* S = smem;                 // [dk][w]
+    float* qv = S + dk * cols;       // [dk]
     float* kv = qv + dk;             // [dk]
     __shared__ float norms[2];
     const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
     int64_t t0, t1;
     seq_span(p, s, t0, t1);
-    const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * dk * dv;
-    for (int e = tid; e < dk * dv; e += blockDim.x)
-        S[e] = state_in ? state_in[head_state + e] : 0.f;
+    const int64_t head_state = (static_cast<int64_t>(s) * p.heads_v + h) * dk * dv + c0;
+    for (int e = tid; e < dk * w; e += blockDim.x) {
+        const int i = e / w, j = e - i * w;
+        S[e] = state_in ? state_in[head_state + static_cast<int64_t>(i) * dv + j] : 0.f;
+    }
     const int hq = h / p.group;
     for (int64_t t = t0; t < t1; ++t) {
         const int64_t qk_off = (t * p.heads_qk + hq) * dk;
@@ -79,24 +86,31 @@ recurrent_generic(Problem p, const T* __restrict__ q, const T* __restrict__ k,
         float gt, bt;
         rule_gates(p, g, beta, gate, h, gt, bt);
         const float decay = __expf(gt);
-        for (int j = tid; j < dv; j += blockDim.x) {
+        for (int j = tid; j < w; j += blockDim.x) {
             float read = 0.f;
             for (int i = 0; i < dk; ++i) {
-                S[i * dv + j] *= decay;
-                read = fmaf(kv[i] * fk, S[i * dv + j], read);
+                S[i * w + j] *= decay;
+                read = fmaf(kv[i] * fk, S[i * w + j], read);
             }
-            const float d = (to_f32(v[(t * p.heads_v + h) * dv + j]) - read) * bt;
+            const float d = (to_f32(v[(t * p.heads_v + h) * dv + c0 + j]) - read) * bt;
             float o = 0.f;
             for (int i = 0; i < dk; ++i) {
-                S[i * dv + j] = fmaf(kv[i] * fk, d, S[i * dv + j]);
-                o = fmaf(qv[i] * fq, S[i * dv + j], o);
+                S[i * w + j] = fmaf(kv[i] * fk, d, S[i * w + j]);
+                o = fmaf(qv[i] * fq, S[i * w + j], o);
             }
-            out[(t * p.heads_v + h) * dv + j] = from_f32<T>(o);
+            out[(t * p.heads_v + h) * dv + c0 + j] = from_f32<T>(o);
         }
         __syncthreads();
     }
-    for (int e = tid; e < dk * dv; e += blockDim.x) state_out[head_state + e] = S[e];
+    for (int e = tid; e < dk * w; e += blockDim.x) {
+        const int i = e / w, j = e - i * w;
+        state_out[head_state + static_cast<int64_t>(i) * dv + j] = S[e];
+    }
 }
+
+// Shared memory of a recurrent_generic CTA is kept under this, so any
+// d_k, d_v <= 256 fits (a 256 x 256 state runs as three column blocks).
+constexpr int kGenericSmemCap = 96 * 1024;
 
 }  // namespace
 
@@ -111,16 +125,21 @@ static cudaError_t launch_recurrent_t(const Problem& p, const void* q, const voi
             p, static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
             beta, state_in, static_cast<T*>(out), state_out);
     } else {
-        const size_t smem = sizeof(float) * (p.d_k * p.d_v + 2 * p.d_k);
+        // Column blocks of equal width, each CTA's state under kGenericSmemCap.
+        const int max_cols = (kGenericSmemCap - 2 * p.d_k * static_cast<int>(sizeof(float))) /
+                             (p.d_k * static_cast<int>(sizeof(float)));
+        const int blocks = (p.d_v + max_cols - 1) / max_cols;
+        const int cols = (p.d_v + blocks - 1) / blocks;
+        const size_t smem = sizeof(float) * (static_cast<size_t>(p.d_k) * cols + 2 * p.d_k);
         if (smem > 48 * 1024) {
             cudaError_t e = cudaFuncSetAttribute(recurrent_generic<T>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(smem));
             if (e != cudaSuccess) return e;
         }
-        recurrent_generic<T><<<grid, 128, smem, stream>>>(
+        recurrent_generic<T><<<dim3(p.heads_v, p.n_seqs, blocks), 128, smem, stream>>>(
             p, static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
-            beta, state_in, static_cast<T*>(out), state_out);
+            beta, state_in, static_cast<T*>(out), state_out, cols);
     }
     return cudaGetLastError();
 }

@@ -117,13 +117,18 @@ def test_chunk_above_64_f32(chunk, eps):
     assert rel_err(o, wo) < TOL_F32 and rel_err(s, ws) < TOL_F32
 
 
-@pytest.mark.parametrize("dk,dv", [(192, 192), (256, 128), (160, 256)])
+@pytest.mark.parametrize("dk,dv", [(192, 192), (256, 128), (160, 256), (256, 256)])
 def test_heads_above_128_chunked_f32(dk, dv):
+    """Head sizes above 128 run on the recurrent kernel, whose CTAs split a
+    state wider than their shared memory into column blocks."""
     x = _inputs([90, 1, 65], torch.float32, hq=1, hv=2, dk=dk, dv=dv, seed=6)
     for algo in ("auto", "cuda_core"):
         o, s = _run("chunked", x, GatedDeltaRule(algo=algo))
         wo, ws = _want("chunked", x)
         assert rel_err(o, wo) < TOL_F32 and rel_err(s, ws) < TOL_F32
+    o, s = _run("recurrent", x, GatedDeltaRule())
+    wo, ws = _want("recurrent", x)
+    assert rel_err(o, wo) < TOL_F32 and rel_err(s, ws) < TOL_F32
 
 
 def test_f16_layer_steps():
