@@ -15,7 +15,7 @@ LIB_PATH = PKG / "libgdr.so"
 GDR_OK, GDR_ERR_INVALID, GDR_ERR_UNSUPPORTED, GDR_ERR_CUDA, GDR_ERR_TIMEOUT = range(5)
 GDR_ERR_CAPACITY = 5
 GDR_MIXED_NOALLOC_MAX_SEQS = 16384
-GDR_DTYPE_F32, GDR_DTYPE_BF16, GDR_DTYPE_F16 = 0, 1, 2
+GDR_DTYPE_F32, GDR_DTYPE_BF16, GDR_DTYPE_F16, GDR_DTYPE_F64 = 0, 1, 2, 3
 GDR_ALGO_AUTO, GDR_ALGO_CUDA_CORE, GDR_ALGO_TENSOR, GDR_ALGO_TENSOR_SPLIT = 0, 1, 2, 3
 
 # Every function include/gdr.h declares, with its ctypes signature.
@@ -70,6 +70,8 @@ _LAYER_ARGS = [ctypes.POINTER(GdrParams), _vp, _vp, _vp, _vp, _vp, ctypes.POINTE
 SIGNATURES = {
     "gdr_recurrent": (_i32, _RULE_ARGS),
     "gdr_chunked": (_i32, _RULE_ARGS),
+    "gdr_recurrent_f64": (_i32, _RULE_ARGS),
+    "gdr_chunked_f64": (_i32, _RULE_ARGS),
     "gdr_chunked_launches": (_i32, [ctypes.POINTER(GdrParams), _i32]),
     "gdr_chunked_host": (_i32, _RULE_ARGS),
     "gdr_chunked_layer": (_i32, _LAYER_ARGS),

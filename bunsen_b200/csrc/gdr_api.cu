@@ -23,6 +23,10 @@ bool split_may_help(const Problem& p);
 cudaError_t launch_chunked_split(const Problem&, const void*, const void*, const void*,
                                  const float*, const float*, const float*, void*, float*, int,
                                  cudaStream_t);
+cudaError_t launch_recurrent_f64(const Problem& p, double eps, const double* q, const double* k,
+                                 const double* v, const double* g, const double* beta,
+                                 const double* state_in, double* out, double* state_out,
+                                 cudaStream_t stream);
 cudaError_t take_device_error(int* flag);
 cudaError_t take_layer_error(int* flag);
 cudaError_t library_pool(cudaMemPool_t* pool, bool create);
@@ -58,13 +62,16 @@ int64_t total_tokens(const Problem& p) {
     return p.cu_seqlens ? p.seq_len : static_cast<int64_t>(p.n_seqs) * p.seq_len;
 }
 
-// Checks what the host can check and fills the kernels' descriptor.
-gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Problem& p) {
+// Checks what the host can check and fills the kernels' descriptor. `f64`:
+// the call is one of the f64 entry points, whose dtype is GDR_DTYPE_F64.
+gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Problem& p,
+                        bool f64 = false) {
     if (params == nullptr) return GDR_ERR_INVALID;
     const gdr_params& a = *params;
     if (a.heads_qk <= 0 || a.heads_v <= 0 || a.heads_v % a.heads_qk != 0) return GDR_ERR_INVALID;
     if (a.d_k <= 0 || a.d_v <= 0 || a.seq_len < 0) return GDR_ERR_INVALID;
-    if (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16 && a.dtype != GDR_DTYPE_F16)
+    if (f64 ? a.dtype != GDR_DTYPE_F64
+            : (a.dtype != GDR_DTYPE_F32 && a.dtype != GDR_DTYPE_BF16 && a.dtype != GDR_DTYPE_F16))
         return GDR_ERR_INVALID;
     if (a.use_l2norm && !(a.l2norm_eps >= 0.0)) return GDR_ERR_INVALID;
     if (cu_seqlens == nullptr && a.batch < 0) return GDR_ERR_INVALID;
@@ -87,8 +94,8 @@ gdr_status make_problem(const gdr_params* params, const int32_t* cu_seqlens, Pro
 
 // Token buffers may be NULL only when there are no tokens (an empty tensor
 // has no storage); the state is written whenever there are sequences.
-bool io_ok(const Problem& p, const void* q, const void* k, const void* v, const float* g,
-           const float* beta, const void* out, const float* state_out) {
+bool io_ok(const Problem& p, const void* q, const void* k, const void* v, const void* g,
+           const void* beta, const void* out, const void* state_out) {
     const bool tokens = total_tokens(p) > 0;
     return (!tokens || (q && k && v && g && beta && out)) && (p.n_seqs == 0 || state_out);
 }
@@ -184,10 +191,34 @@ gdr_status gdr_recurrent(const gdr_params* params, const void* q, const void* k,
     gdr_status st = make_problem(params, cu_seqlens, p);
     if (st != GDR_OK) return st;
     if (!io_ok(p, q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
-    if (p.d_k > 256 || p.d_v > 256) return GDR_ERR_UNSUPPORTED;
+    if (p.d_k > kRecurrentMaxD || p.d_v > kRecurrentMaxD) return GDR_ERR_UNSUPPORTED;
     if (p.n_seqs == 0) return GDR_OK;
     return from_cuda(gdr::launch_recurrent(p, params->dtype, q, k, v, g, beta, state_in, out,
                                            state_out, static_cast<cudaStream_t>(stream)));
+}
+
+gdr_status gdr_recurrent_f64(const gdr_params* params, const double* q, const double* k,
+                             const double* v, const double* g, const double* beta,
+                             const double* state_in, double* out, double* state_out,
+                             const int32_t* cu_seqlens, void* stream) {
+    Problem p;
+    gdr_status st = make_problem(params, cu_seqlens, p, true);
+    if (st != GDR_OK) return st;
+    if (!io_ok(p, q, k, v, g, beta, out, state_out)) return GDR_ERR_INVALID;
+    if (p.d_k > kRecurrentMaxD || p.d_v > kRecurrentMaxD) return GDR_ERR_UNSUPPORTED;
+    if (p.n_seqs == 0) return GDR_OK;
+    return from_cuda(gdr::launch_recurrent_f64(p, params->l2norm_eps, q, k, v, g, beta, state_in,
+                                               out, state_out,
+                                               static_cast<cudaStream_t>(stream)));
+}
+
+gdr_status gdr_chunked_f64(const gdr_params* params, const double* q, const double* k,
+                           const double* v, const double* g, const double* beta,
+                           const double* state_in, double* out, double* state_out,
+                           const int32_t* cu_seqlens, void* stream) {
+    if (params != nullptr && params->chunk_size <= 0) return GDR_ERR_INVALID;  // delta_rule.rs:233
+    return gdr_recurrent_f64(params, q, k, v, g, beta, state_in, out, state_out, cu_seqlens,
+                             stream);
 }
 
 gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, const void* v,

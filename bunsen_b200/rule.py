@@ -12,6 +12,10 @@ reads key head ``h // (H_v // H_qk)``, the arithmetic of the
 ``repeat_interleave`` bunsen's caller applies, ``gated_delta_net.rs:404-419``),
 and a packed ragged batch ``[T_total, H, .]`` with ``cu_seqlens``.
 
+f64 inputs compute in f64, g, beta and the state included, as bunsen does
+when its inputs are f64 (``burner/tensor/widening.rs:58-60``); the other
+dtypes return an f32 state.
+
 Every call runs a CUDA kernel of ``libgdr.so``; there is no other path.
 """
 
@@ -116,6 +120,8 @@ class GatedDeltaRule:
         if gates is not None or norm is not None:
             io, keep, g, beta = _layer_io(gates, norm, q, v, g, beta)
         check_shapes(q, k, v, g, beta, None, cu_seqlens)
+        if q.dtype not in _DTYPES:
+            raise TypeError(f"a continuous batch takes f32, bf16 or f16 q, k, v, not {q.dtype}")
         dev = q.device
         if dev.type != "cuda":
             raise RuntimeError("libgdr runs on CUDA tensors only")
@@ -222,11 +228,17 @@ class GatedDeltaRule:
             batch=b, seq_len=t, n_seqs=n, heads_qk=h_qk, heads_v=v.shape[-2], d_k=d_k,
             d_v=v.shape[-1], chunk_size=self.chunk_size,
             use_l2norm=int(self.qk_l2norm_eps is not None),
-            l2norm_eps=float(self.qk_l2norm_eps or 0.0), dtype=_DTYPES[q.dtype],
+            l2norm_eps=float(self.qk_l2norm_eps or 0.0),
+            dtype=_lib.GDR_DTYPE_F64 if q.dtype == torch.float64 else _DTYPES[q.dtype],
             algo=_ALGOS[self.algo], split_chunks=self.split_chunks)
 
     def _run(self, fn, q, k, v, g, beta, state, cu_seqlens, out, state_out, gates=None,
              norm=None):
+        if q.dtype == torch.float64:
+            if gates is not None or norm is not None:
+                raise TypeError("the layer's gates and norm take f32, bf16 or f16 tensors")
+            return self._run_f64(fn + "_f64", q, k, v, g, beta, state, cu_seqlens, out,
+                                 state_out)
         packed = cu_seqlens is not None
         lead = 1 if packed else 2
         io, keep = None, []
@@ -261,6 +273,38 @@ class GatedDeltaRule:
                 out.data_ptr(), state_out.data_ptr(), _ptr(cu_seqlens), _stream(dev))
             _lib.check(fn + "_layer", status)
             return out, state_out
+        status = getattr(_lib.load(), fn)(
+            ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
+            beta.data_ptr(), _ptr(state), out.data_ptr(), state_out.data_ptr(),
+            _ptr(cu_seqlens), _stream(dev))
+        _lib.check(fn, status)
+        return out, state_out
+
+
+    def _run_f64(self, fn, q, k, v, g, beta, state, cu_seqlens, out, state_out):
+        """f64 inputs: every tensor (g, beta, states, out) in f64."""
+        packed = cu_seqlens is not None
+        lead = 1 if packed else 2
+        check_shapes(q, k, v, g, beta, state, cu_seqlens)
+        dev = q.device
+        if dev.type != "cuda":
+            raise RuntimeError("libgdr runs on CUDA tensors only")
+        f64 = torch.float64
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        g, beta = g.to(f64).contiguous(), beta.to(f64).contiguous()
+        n = (cu_seqlens.numel() - 1) if packed else q.shape[0]
+        h_v, d_k, d_v = v.shape[-2], q.shape[-1], v.shape[-1]
+        if out is None:
+            out = torch.empty(v.shape[:lead] + (h_v, d_v), dtype=f64, device=dev)
+        if state_out is None:
+            state_out = torch.empty((n, h_v, d_k, d_v), dtype=f64, device=dev)
+        if out.dtype != f64 or state_out.dtype != f64:
+            raise TypeError("an f64 call writes f64 outputs and states")
+        if state is not None:
+            state = state.to(f64).contiguous()
+        if packed:
+            cu_seqlens = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+        p = self.params(q, v, cu_seqlens)
         status = getattr(_lib.load(), fn)(
             ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
             beta.data_ptr(), _ptr(state), out.data_ptr(), state_out.data_ptr(),

@@ -44,7 +44,7 @@
  *  - dtypes: q, k, v share `params->dtype`; `out` is written in that dtype
  *    (bunsen narrows the output to q's dtype, delta_rule.rs:207, 304). g,
  *    beta and the states are f32, the dtype the rule runs in
- *    (burner/tensor/widening.rs:60).
+ *    (burner/tensor/widening.rs:60); f64 in the f64 entry points.
  *  - `state_in` may be NULL (zeros, delta_rule.rs:330). `state_out` may equal
  *    `state_in` (an in-place update); bunsen itself never writes into a state
  *    (linear_attention/state.rs:201-204), so a caller that shares states must
@@ -63,7 +63,7 @@
 extern "C" {
 #endif
 
-#define GDR_ABI_VERSION 2
+#define GDR_ABI_VERSION 3
 
 typedef enum gdr_status {
     GDR_OK = 0,
@@ -78,11 +78,13 @@ typedef enum gdr_status {
  * (burner/tensor/widening.rs:58-60) and narrows the output back: bf16 runs
  * take bf16 operands on the tensor cores with f32 accumulation; f16 runs
  * compute in f32 on the CUDA-core kernels, as f32 runs do. f64, which bunsen
- * keeps as its compute dtype, is not served. */
+ * keeps as its compute dtype (g, beta and the state included), has its own
+ * entry points, gdr_recurrent_f64 and gdr_chunked_f64. */
 typedef enum gdr_dtype {
     GDR_DTYPE_F32 = 0,
     GDR_DTYPE_BF16 = 1,
-    GDR_DTYPE_F16 = 2
+    GDR_DTYPE_F16 = 2,
+    GDR_DTYPE_F64 = 3  /* gdr_recurrent_f64 / gdr_chunked_f64 only */
 } gdr_dtype;
 
 /* Which kernel family runs a chunked call. AUTO picks the tensor-core kernels
@@ -134,6 +136,21 @@ gdr_status gdr_recurrent(const gdr_params* params, const void* q, const void* k,
 gdr_status gdr_chunked(const gdr_params* params, const void* q, const void* k, const void* v,
                        const float* g, const float* beta, const float* state_in, void* out,
                        float* state_out, const int32_t* cu_seqlens, void* stream);
+
+/* The two forms for f64 inputs (params->dtype = GDR_DTYPE_F64): q, k, v, g,
+ * beta, out and both states in f64, every product in f64 on the CUDA cores,
+ * as bunsen computes when its inputs are f64 (widening.rs:58-60 keeps f64).
+ * Both run the recurrent kernel: the chunked form is the same rule, equal to
+ * the recurrent one up to rounding (delta_rule.rs:549-608), so the chunk size
+ * is checked (> 0) but changes nothing. Any d_k, d_v up to 256. */
+gdr_status gdr_recurrent_f64(const gdr_params* params, const double* q, const double* k,
+                             const double* v, const double* g, const double* beta,
+                             const double* state_in, double* out, double* state_out,
+                             const int32_t* cu_seqlens, void* stream);
+gdr_status gdr_chunked_f64(const gdr_params* params, const double* q, const double* k,
+                           const double* v, const double* g, const double* beta,
+                           const double* state_in, double* out, double* state_out,
+                           const int32_t* cu_seqlens, void* stream);
 
 /* gdr_chunked on HOST buffers: every pointer (cu_seqlens included) is host
  * memory, pinned for the copies to overlap. The call copies groups of whole

@@ -22,7 +22,8 @@
 namespace bunsen_b200 {
 
 // A contiguous device tensor: q, k [B, T, H_qk, d_k]; v, out [B, T, H_v, d_v];
-// g, beta [B, T, H_v] (f32); state [B, H_v, d_k, d_v] (f32).
+// g, beta [B, T, H_v] (f32); state [B, H_v, d_k, d_v] (f32). With dtype
+// GDR_DTYPE_F64 every tensor is f64, g, beta and the states included.
 struct View {
     void* data = nullptr;
     int64_t dims[4] = {0, 0, 0, 0};
@@ -111,11 +112,20 @@ struct GatedDeltaRule {
         p.dtype = dtype;
         p.algo = algo;
         p.split_chunks = split_chunks;
-        const auto fn = chunked_form ? gdr_chunked : gdr_recurrent;
-        const gdr_status st =
-            fn(&p, q.data, k.data, v.data, static_cast<const float*>(g.data),
-               static_cast<const float*>(beta.data), static_cast<const float*>(state.data),
-               out.data, static_cast<float*>(state_out.data), nullptr, stream);
+        gdr_status st;
+        if (dtype == GDR_DTYPE_F64) {
+            const auto fn = chunked_form ? gdr_chunked_f64 : gdr_recurrent_f64;
+            st = fn(&p, static_cast<const double*>(q.data), static_cast<const double*>(k.data),
+                    static_cast<const double*>(v.data), static_cast<const double*>(g.data),
+                    static_cast<const double*>(beta.data), static_cast<const double*>(state.data),
+                    static_cast<double*>(out.data), static_cast<double*>(state_out.data), nullptr,
+                    stream);
+        } else {
+            const auto fn = chunked_form ? gdr_chunked : gdr_recurrent;
+            st = fn(&p, q.data, k.data, v.data, static_cast<const float*>(g.data),
+                    static_cast<const float*>(beta.data), static_cast<const float*>(state.data),
+                    out.data, static_cast<float*>(state_out.data), nullptr, stream);
+        }
         if (st == GDR_ERR_INVALID) throw std::invalid_argument(gdr_status_string(st));
         if (st != GDR_OK) throw std::runtime_error(gdr_status_string(st));
     }

@@ -54,7 +54,7 @@ def test_params_layout_matches_header(tmp_path):
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.gdr_abi_version() == 2
+    assert lib.gdr_abi_version() == 3
     for s in range(5):
         assert lib.gdr_status_string(s)
     assert lib.gdr_status_string(99) == b"unknown status"
@@ -157,6 +157,24 @@ def test_dtype_and_shape_routes():
     ws = ctypes.c_void_p(16)
     assert lib.gdr_mixed(ctypes.byref(p), d, d, d, d, d, d, None, 1, d, cu, ws, 1 << 20,
                          None) == _lib.GDR_ERR_UNSUPPORTED
+
+
+def test_f64_entry_points_check_before_any_launch():
+    """The f64 forms take only GDR_DTYPE_F64 (and the other entry points never
+    take it), refuse a zero chunk like bunsen (delta_rule.rs:233) and heads
+    above 256; all before any CUDA call."""
+    lib = _lib.load()
+    d = ctypes.c_void_p(16)
+    args = lambda p: (ctypes.byref(p), d, d, d, d, d, None, d, d, None, None)  # noqa: E731
+    f64 = dict(batch=2, seq_len=8, d_k=32, d_v=32, dtype=_lib.GDR_DTYPE_F64)
+    for fn in (lib.gdr_recurrent_f64, lib.gdr_chunked_f64):
+        assert fn(*args(_params(**dict(f64, dtype=_lib.GDR_DTYPE_F32)))) == _lib.GDR_ERR_INVALID
+        assert fn(*args(_params(**dict(f64, d_v=257)))) == _lib.GDR_ERR_UNSUPPORTED
+        assert fn(*args(_params(**dict(f64, heads_v=3)))) == _lib.GDR_ERR_INVALID
+    assert lib.gdr_chunked_f64(*args(_params(**dict(f64, chunk_size=0)))) == _lib.GDR_ERR_INVALID
+    for fn in (lib.gdr_recurrent, lib.gdr_chunked):
+        assert fn(*args(_params(**f64))) == _lib.GDR_ERR_INVALID
+    assert lib.gdr_chunked_launches(ctypes.byref(_params(**f64)), 0) == -1
 
 
 def test_host_call_rejects_malformed_offsets_before_any_copy():

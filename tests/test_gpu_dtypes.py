@@ -195,3 +195,55 @@ def test_bf16_inputs_on_the_f32_kernel():
     o, s = _run("chunked", x, GatedDeltaRule(algo="cuda_core"))
     wo, ws = _want("chunked", x)
     assert rel_err(o, wo) < 1e-2 and rel_err(s, ws) < TOL_F32
+
+
+TOL_F64 = 1e-10
+
+
+@pytest.mark.parametrize("form", ["chunked", "recurrent"])
+@pytest.mark.parametrize("dk,dv", [(8, 12), (128, 128), (256, 256)])
+@pytest.mark.parametrize("eps", [1e-6, None])
+def test_f64_against_the_scalar_f64_rule(form, dk, dv, eps):
+    """f64 inputs compute in f64 (bunsen keeps f64 as its compute dtype, g,
+    beta and the state included), held to the f64 scalar rule of bunsen's
+    tests (delta_rule.rs:399-445) at 1e-10; a 256 x 256 state runs as column
+    blocks."""
+    lens = [70, 1, 0, 33]
+    x = _inputs(lens, torch.float64, hq=1, hv=2, dk=dk, dv=dv, seed=10)
+    x["g"], x["beta"], x["state"] = (x[n].double() for n in ("g", "beta", "state"))
+    if eps is None:  # keep the rule stable without the norm
+        x["k"] = x["k"] * 0.9
+    rule = GatedDeltaRule(qk_l2norm_eps=eps)
+    o, s = getattr(rule, form)(x["q"], x["k"], x["v"], x["g"], x["beta"], x["state"],
+                               cu_seqlens=x["cu_seqlens"])
+    _ok()
+    assert o.dtype == torch.float64 and s.dtype == torch.float64
+    wo, ws = oracle.scalar_f64(*(x[n].cpu().numpy() for n in ("q", "k", "v", "g", "beta")),
+                               x["state"].cpu().numpy(), l2norm_eps=eps,
+                               cu_seqlens=x["cu_seqlens"].cpu().numpy().astype(np.int32))
+    assert rel_err(o.cpu().numpy(), wo) < TOL_F64 and rel_err(s.cpu().numpy(), ws) < TOL_F64
+
+
+def test_f64_dense_batch_and_refusals():
+    """A dense f64 batch through both forms (the chunk size changes nothing);
+    f64 with the layer's gates or in a continuous batch is refused."""
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    f = dict(device=DEV, generator=gen, dtype=torch.float64)
+    b, t, h, d = 2, 37, 2, 16
+    q, k, v = (torch.randn(b, t, h, d, **f) for _ in range(3))
+    g = torch.log(torch.rand(b, t, h, **f) * 0.099 + 0.9)
+    beta = torch.sigmoid(torch.randn(b, t, h, **f))
+    s0 = torch.randn(b, h, d, d, **f) * 0.1
+    o1, s1 = GatedDeltaRule(chunk_size=16).chunked(q, k, v, g, beta, s0)
+    o2, s2 = GatedDeltaRule().recurrent(q, k, v, g, beta, s0)
+    _ok()
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    wo, ws = oracle.scalar_f64(*(x.cpu().numpy() for x in (q, k, v, g, beta, s0)))
+    assert rel_err(o1.cpu().numpy(), wo) < TOL_F64 and rel_err(s1.cpu().numpy(), ws) < TOL_F64
+    with pytest.raises(TypeError):
+        GatedDeltaRule().chunked(q, k, v, None, None, s0, gates=(g, beta, g[0, 0], g[0, 0]))
+    cu = torch.tensor([0, t, 2 * t], dtype=torch.int32, device=DEV)
+    pool = torch.zeros(2, h, d, d, device=DEV)
+    with pytest.raises(TypeError):
+        GatedDeltaRule().mixed(q.reshape(-1, h, d), k.reshape(-1, h, d), v.reshape(-1, h, d),
+                               g.reshape(-1, h), beta.reshape(-1, h), pool, cu_seqlens=cu)
