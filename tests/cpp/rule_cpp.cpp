@@ -1,5 +1,6 @@
 // The C++ face of the ABI (include/gdr.hpp): shape contracts throw like bunsen's
-// panics, and on a GPU the chunked form agrees with the recurrent form.
+// panics, and on a GPU the chunked form agrees with the recurrent form (f32,
+// and f64 computed in f64).
 //   rule_cpp contracts   -- no GPU needed
 //   rule_cpp parity      -- runs both forms on cuda:0
 #include <cuda_runtime.h>
@@ -94,9 +95,43 @@ static int parity() {
         return m / s;
     };
     const double eo = rel(h1, h2), es = rel(hs1, hs2);
-    const bool ok = cudaGetLastError() == cudaSuccess && eo < 1e-4 && es < 1e-4;
+    bool ok = cudaGetLastError() == cudaSuccess && eo < 1e-4 && es < 1e-4;
     std::printf("parity: out %.2e state %.2e %s\n", eo, es, ok ? "ok" : "FAIL");
-    return ok ? 0 : 1;
+
+    // f64: every tensor in f64 (bunsen's compute dtype for f64 inputs); both
+    // forms run one kernel, so they agree exactly, and the f32 run to 1e-4.
+    auto up64 = [](const std::vector<float>& h) {
+        const std::vector<double> w(h.begin(), h.end());
+        double* p = nullptr;
+        cudaMalloc(&p, w.size() * sizeof(double));
+        cudaMemcpy(p, w.data(), w.size() * sizeof(double), cudaMemcpyHostToDevice);
+        return p;
+    };
+    double *eq = up64(q), *ek = up64(k), *ev = up64(v), *eg = up64(g), *eb = up64(beta),
+           *es0 = up64(s0);
+    double *p1, *p2, *t1, *t2;
+    cudaMalloc(&p1, v.size() * 8);
+    cudaMalloc(&p2, v.size() * 8);
+    cudaMalloc(&t1, s0.size() * 8);
+    cudaMalloc(&t2, s0.size() * 8);
+    GatedDeltaRule r64 = rule;
+    r64.dtype = GDR_DTYPE_F64;
+    auto Q8 = view(eq, {B, T, Hq, D}), K8 = view(ek, {B, T, Hq, D}), V8 = view(ev, {B, T, Hv, D});
+    auto G8 = view(eg, {B, T, Hv}), Be8 = view(eb, {B, T, Hv}), S8 = view(es0, {B, Hv, D, D});
+    r64.chunked(Q8, K8, V8, G8, Be8, S8, view(p1, {B, T, Hv, D}), view(t1, {B, Hv, D, D}));
+    r64.recurrent(Q8, K8, V8, G8, Be8, S8, view(p2, {B, T, Hv, D}), view(t2, {B, Hv, D, D}));
+    std::vector<double> d1(v.size()), d2(v.size()), ds1(s0.size()), ds2(s0.size());
+    cudaMemcpy(d1.data(), p1, d1.size() * 8, cudaMemcpyDeviceToHost);
+    cudaMemcpy(d2.data(), p2, d2.size() * 8, cudaMemcpyDeviceToHost);
+    cudaMemcpy(ds1.data(), t1, ds1.size() * 8, cudaMemcpyDeviceToHost);
+    cudaMemcpy(ds2.data(), t2, ds2.size() * 8, cudaMemcpyDeviceToHost);
+    const std::vector<float> f1(d1.begin(), d1.end()), fs1(ds1.begin(), ds1.end());
+    const double e64o = rel(f1, h2), e64s = rel(fs1, hs2);
+    const bool ok64 = cudaGetLastError() == cudaSuccess && d1 == d2 && ds1 == ds2 &&
+                      e64o < 1e-4 && e64s < 1e-4;
+    std::printf("f64: forms equal %d, against f32 out %.2e state %.2e %s\n",
+                static_cast<int>(d1 == d2 && ds1 == ds2), e64o, e64s, ok64 ? "ok" : "FAIL");
+    return ok && ok64 ? 0 : 1;
 }
 
 int main(int argc, char** argv) {
