@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from bunsen_b200 import _lib
-from bunsen_b200.layer import causal_conv1d, state_reorder
+from bunsen_b200.layer import causal_conv1d, gated_norm, state_reorder
 from bunsen_b200.rule import GatedDeltaRule
 from oracle import layer as olayer
 from tests.conftest import TOL_BF16_OUT, TOL_BF16_STATE, TOL_F32, rel_err
@@ -289,6 +289,25 @@ def test_conv_silu_elementwise_over_the_negative_range():
     got = _np(y)[0]
     err = np.abs(got - want)
     assert np.all(err <= 1e-2 * np.abs(want)), float((err / np.maximum(np.abs(want), 1e-30)).max())
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 5, 4099])
+def test_gated_norm_bf16_128_rows_and_in_place(rows):
+    """The standalone gated norm's bf16, 128-feature kernel (two rows per
+    warp instruction, four per warp): row counts that leave a warp partly
+    empty, element by element against the oracle, and in place (out = x)."""
+    gen = torch.Generator(device=DEV).manual_seed(rows)
+    x = torch.randn(rows, 128, device=DEV, generator=gen).bfloat16()
+    z = (torch.randn(rows, 128, device=DEV, generator=gen) * 3).bfloat16()
+    w = torch.rand(128, device=DEV, generator=gen) + 0.5
+    want = olayer.gated_norm(_np(x), _np(z), _np(w), 1e-6)
+    y = gated_norm(x, z, w, 1e-6)
+    _ok()
+    err = np.abs(_np(y) - want)
+    assert np.all(err <= 1e-2 * np.abs(want) + 1e-6), float(err.max())
+    y2 = gated_norm(x, z, w, 1e-6, out=x)
+    _ok()
+    assert y2.data_ptr() == x.data_ptr() and torch.equal(y2, y)
 
 
 def test_fused_norm_elementwise_against_the_plain_prefill():
