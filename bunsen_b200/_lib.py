@@ -16,6 +16,7 @@ GDR_OK, GDR_ERR_INVALID, GDR_ERR_UNSUPPORTED, GDR_ERR_CUDA, GDR_ERR_TIMEOUT = ra
 GDR_ERR_CAPACITY = 5
 GDR_MIXED_NOALLOC_MAX_SEQS = 16384
 GDR_DTYPE_F32, GDR_DTYPE_BF16, GDR_DTYPE_F16, GDR_DTYPE_F64 = 0, 1, 2, 3
+ABI_VERSION = 3  # GDR_ABI_VERSION of include/gdr.h these bindings follow
 GDR_ALGO_AUTO, GDR_ALGO_CUDA_CORE, GDR_ALGO_TENSOR, GDR_ALGO_TENSOR_SPLIT = 0, 1, 2, 3
 
 # Every function include/gdr.h declares, with its ctypes signature.

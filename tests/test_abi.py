@@ -52,9 +52,16 @@ def test_params_layout_matches_header(tmp_path):
     assert got == want
 
 
+def test_binding_version_matches_the_header():
+    """The bindings' ABI_VERSION is include/gdr.h's GDR_ABI_VERSION (build()
+    checks the loaded library against it)."""
+    text = HEADER.read_text()
+    assert int(re.search(r"#define GDR_ABI_VERSION (\d+)", text).group(1)) == _lib.ABI_VERSION
+
+
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.gdr_abi_version() == 3
+    assert lib.gdr_abi_version() == _lib.ABI_VERSION == 3
     for s in range(5):
         assert lib.gdr_status_string(s)
     assert lib.gdr_status_string(99) == b"unknown status"
