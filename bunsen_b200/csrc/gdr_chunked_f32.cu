@@ -5,10 +5,13 @@
 // which it widens to f32, burner/tensor/widening.rs:58-60). One CTA of 256
 // threads per (sequence, value head) walks the sequence's chunks with the
 // [128, 128] state in shared memory. Each product of a chunk is register-
-// tiled: a thread owns a 4 x 8 (or 8 x 8) block of the result, rows strided
-// by 16 and columns in two groups of four, so each k step loads a few scalars
-// and two 16-byte vectors for 32 or 64 FMAs, and a warp's vector loads cover
-// consecutive 16-byte pieces of one row (no bank conflicts).
+// tiled: a thread owns a 4 x 8 (or 8 x 8) block of the result, consecutive
+// rows and columns in two groups of four. The left operands that a k step
+// reads down a column (the inverse X and the intra matrix) are kept
+// transposed, so each k step loads one or two 16-byte vectors of them (a few
+// scalars where the operand is row-major) and two 16-byte vectors of the right
+// operand for 32 or 64 FMAs; a warp's vector loads cover consecutive 16-byte
+// pieces of one row (no bank conflicts).
 //
 // Per chunk of C = 64 positions (zero-padded past the sequence end, where
 // g = beta = 0 and nothing is written, delta_rule.rs:241-262):
@@ -117,7 +120,7 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
     F32Smem& sm = *reinterpret_cast<F32Smem*>(f32_smem_raw);
     const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int ti = tid >> 4, tj = tid & 15;  // rows ti + 16 a, columns n0 .. and n0 + 64 ..
+    const int ti = tid >> 4, tj = tid & 15;  // rows 4 ti + a, columns n0 .. and n0 + 64 ..
     const int n0 = 4 * tj;
     int64_t t0, t1;
     seq_span(p, s, t0, t1);
@@ -224,7 +227,7 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
                     const int i = ti + 16 * a, j = tj + 16 * b;
                     const float dec = j <= i ? __expf(sm.gam[i] - sm.gam[j]) : 0.f;
                     sm.A[i * kLc + j] = j < i ? -(sm.bet[i] * kk[a][b]) * dec : 0.f;
-                    sm.I[i * kLc + j] = qk[a][b] * dec;
+                    sm.I[j * kLc + i] = qk[a][b] * dec;  // transposed: I^T
                 }
         }
         __syncthreads();
@@ -241,31 +244,31 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
                     for (int r = s2 + 1; r < kC; ++r) xc[r] = fmaf(sm.A[r * kLc + s2], xc[s2], xc[r]);
             }
             __syncthreads();
-            if (tid < kC) {
+            if (tid < kC) {  // X^T: column tid of X is row tid here
 #pragma unroll
-                for (int r = 0; r < kC; ++r) sm.A[r * kLc + tid] = xc[r];
+                for (int r = 0; r < kC; r += 4)
+                    store4(sm.A + tid * kLc + r, make_float4(xc[r], xc[r + 1], xc[r + 2], xc[r + 3]));
             }
         }
         __syncthreads();
         // 4. U = X (beta V) and W = X diag(beta e^gamma) K, this thread's rows
-        //    ti + 16 a and columns n0 .. n0 + 3, n0 + 64 .. n0 + 67.
+        //    4 ti .. 4 ti + 3 and columns n0 .. n0 + 3, n0 + 64 .. n0 + 67.
         float u[4][8] = {}, w[4][8] = {};
 #pragma unroll 4
         for (int j = 0; j < kC; ++j) {
-            float xa[4], xw[4];
             const float wj = sm.wf[j];
+            const float4 x4 = *reinterpret_cast<const float4*>(sm.A + j * kLc + 4 * ti);
+            const float xa[4] = {x4.x, x4.y, x4.z, x4.w};
+            float xw[4];
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
-                xa[a] = sm.A[(ti + 16 * a) * kLc + j];
-                xw[a] = xa[a] * wj;
-            }
+            for (int a = 0; a < 4; ++a) xw[a] = xa[a] * wj;
             fma_4x8(u, xa, sm.V + j * kLd, n0);
             fma_4x8(w, xw, sm.K + j * kLd, n0);
         }
         __syncthreads();  // beta V is read: W goes into its buffer
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
-            float* row = sm.V + (ti + 16 * a) * kLd;
+            float* row = sm.V + (4 * ti + a) * kLd;
             store4(row + n0, make_float4(w[a][0], w[a][1], w[a][2], w[a][3]));
             store4(row + n0 + 64, make_float4(w[a][4], w[a][5], w[a][6], w[a][7]));
         }
@@ -279,15 +282,15 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
                 float qa[4], wa[4];
 #pragma unroll
                 for (int a = 0; a < 4; ++a) {
-                    qa[a] = sm.Q[(ti + 16 * a) * kLd + x];
-                    wa[a] = sm.V[(ti + 16 * a) * kLd + x];
+                    qa[a] = sm.Q[(4 * ti + a) * kLd + x];
+                    wa[a] = sm.V[(4 * ti + a) * kLd + x];
                 }
                 fma_4x8(o, qa, sm.S + x * kLd, n0);
                 fma_4x8(ws, wa, sm.S + x * kLd, n0);
             }
 #pragma unroll
             for (int a = 0; a < 4; ++a) {
-                const float eg = sm.eg[ti + 16 * a];
+                const float eg = sm.eg[4 * ti + a];
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     u[a][c] -= ws[a][c];
@@ -298,7 +301,7 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
         __syncthreads();  // Q and W are read: V_new goes into Q's buffer
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
-            float* row = sm.Q + (ti + 16 * a) * kLd;
+            float* row = sm.Q + (4 * ti + a) * kLd;
             store4(row + n0, make_float4(u[a][0], u[a][1], u[a][2], u[a][3]));
             store4(row + n0 + 64, make_float4(u[a][4], u[a][5], u[a][6], u[a][7]));
         }
@@ -306,27 +309,26 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
         // 7. O = (e^gamma Q) S + intra V_new (rows past the end dropped) ...
 #pragma unroll 4
         for (int j = 0; j < kC; ++j) {
-            float ia[4];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) ia[a] = sm.I[(ti + 16 * a) * kLc + j];
+            const float4 i4 = *reinterpret_cast<const float4*>(sm.I + j * kLc + 4 * ti);
+            const float ia[4] = {i4.x, i4.y, i4.z, i4.w};
             fma_4x8(o, ia, sm.Q + j * kLd, n0);
         }
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
-            const int i = ti + 16 * a;
+            const int i = 4 * ti + a;
             if (i < valid) {
                 T* dst = out + ((base + i) * p.heads_v + h) * kD;
                 store4(dst + n0, make_float4(o[a][0], o[a][1], o[a][2], o[a][3]));
                 store4(dst + n0 + 64, make_float4(o[a][4], o[a][5], o[a][6], o[a][7]));
             }
         }
-        // ... and S <- e^gamma_C S + (K e^(gamma_C - gamma))^T V_new, rows ti + 16 a.
+        // ... and S <- e^gamma_C S + (K e^(gamma_C - gamma))^T V_new, rows 8 ti .. 8 ti + 7.
         {
             const float decay = __expf(sm.gam[kC - 1]);
             float st[8][8];
 #pragma unroll
             for (int a = 0; a < 8; ++a) {
-                const float* row = sm.S + (ti + 16 * a) * kLd;
+                const float* row = sm.S + (8 * ti + a) * kLd;
                 const float4 b0 = *reinterpret_cast<const float4*>(row + n0);
                 const float4 b1 = *reinterpret_cast<const float4*>(row + n0 + 64);
                 st[a][0] = b0.x * decay; st[a][1] = b0.y * decay;
@@ -336,15 +338,16 @@ chunked_f32_d128(Problem p, const T* __restrict__ q, const T* __restrict__ k,
             }
 #pragma unroll 2
             for (int r = 0; r < kC; ++r) {
-                float ka[8];
                 const float f = sm.rr[r];
-#pragma unroll
-                for (int a = 0; a < 8; ++a) ka[a] = sm.K[r * kLd + ti + 16 * a] * f;
+                const float4 k0 = *reinterpret_cast<const float4*>(sm.K + r * kLd + 8 * ti);
+                const float4 k1 = *reinterpret_cast<const float4*>(sm.K + r * kLd + 8 * ti + 4);
+                const float ka[8] = {k0.x * f, k0.y * f, k0.z * f, k0.w * f,
+                                     k1.x * f, k1.y * f, k1.z * f, k1.w * f};
                 fma_8x8(st, ka, sm.Q + r * kLd, n0);
             }
 #pragma unroll
             for (int a = 0; a < 8; ++a) {
-                float* row = sm.S + (ti + 16 * a) * kLd;
+                float* row = sm.S + (8 * ti + a) * kLd;
                 store4(row + n0, make_float4(st[a][0], st[a][1], st[a][2], st[a][3]));
                 store4(row + n0 + 64, make_float4(st[a][4], st[a][5], st[a][6], st[a][7]));
             }
