@@ -1217,7 +1217,8 @@ mixed_tc(const Problem p, const __grid_constant__ CUtensorMap tm_q,
 //           is the sequence's).
 // A middle segment runs three times, so the plan weighs the longest chain
 // against the extra work and splits nothing when the chain does not bound the
-// call.
+// call. Two segments need neither B/M runs nor a scan link: pass B's segment
+// starts from the state pass A's first segment ends in.
 enum : int32_t { kRunFull = 0, kRunSeg0 = 1, kRunB = 2, kRunM = 3, kRunMid = 4, kRunLast = 5 };
 
 struct SplitDesc {
@@ -1243,12 +1244,14 @@ constexpr int kScanBlocks = 8;          // column blocks of a (sequence, head) s
 
 // A pass of `n` items (`work` chunk-times in all, the longest `longest`) on
 // `slots` CTA slots, as the longest-first list schedule runs it: one wave
-// when the items fit the slots, else about half the longest beyond the
-// average load.
+// when the items fit the slots, else the longest item or the average load
+// plus half an average item, whichever is more (a replay of that schedule on
+// the ragged pack's passes at 2 to 32 value heads agrees within a few
+// chunk-times).
 __device__ __forceinline__ float pass_time(float n, float work, float longest, float slots) {
     if (n <= 0.f) return 0.f;
     if (n <= slots) return longest * (n <= 0.5f * slots ? kAloneFactor : 1.f);
-    return fmaxf(work / slots + 0.5f * longest, longest);
+    return fmaxf(work / slots + 0.5f * work / n, longest);
 }
 
 __device__ __forceinline__ int seg_begin(int c, int parts, int i) {
@@ -1336,7 +1339,7 @@ plan_split(const Problem p, int32_t* work, SplitDesc* da, SplitDesc* db, int4* s
         for (int s = lane; s < n; s += 32) {
             const int c = chunks_of(s);
             const int parts = L > 0 ? (c + L - 1) / L : 1;
-            if (parts < 3) {
+            if (parts < 2) {
                 wa += c + kItemCost;
                 ma = fmaxf(ma, c + kItemCost);
                 na += 1;
@@ -1410,7 +1413,7 @@ plan_split(const Problem p, int32_t* work, SplitDesc* da, SplitDesc* db, int4* s
     auto parts_of = [&](int c) { return L > 0 ? (c + L - 1) / L : 1; };
     for (int s = tid; s < n; s += blockDim.x) {  // count the items by length
         const int c = chunks_of(s), parts = parts_of(c);
-        if (parts < 3) {
+        if (parts < 2) {
             atomicAdd(&hist[0][bucket(c)], 1);
             continue;
         }
@@ -1431,7 +1434,7 @@ plan_split(const Problem p, int32_t* work, SplitDesc* da, SplitDesc* db, int4* s
     exclusive_scan_1024(hist[2], warp_sums);  // split sequences, longest first
     for (int s = tid; s < n; s += blockDim.x) {  // place them
         const int c = chunks_of(s), parts = parts_of(c);
-        if (parts < 3) {
+        if (parts < 2) {
             da[atomicAdd(&hist[0][bucket(c)], 1)] = SplitDesc{s, 0, -1, kRunFull};
             continue;
         }
@@ -1609,6 +1612,7 @@ split_scan(int32_t* work, const int4* splits, float* scratch, int seg_cap, int H
         const int h = jh % H;
         const int4 sp = splits[jh / H];
         const int base = sp.x, parts = sp.y;
+        if (parts < 3) continue;  // two segments: no link (every thread sees the same item)
         const int col0 = cb * kScanCols;
         {
             const float* x1 = split_state(scratch, seg_cap, H, 0, base + 1, h);
@@ -1906,8 +1910,8 @@ SplitShape split_shape(const Problem& p, int forced) {
                                         : static_cast<int64_t>(p.n_seqs) * sh.max_chunks;
     const double avg = static_cast<double>(chunks) * p.heads_v / sh.slots;
     sh.l_min = forced > 0 ? forced : std::max(kMinSegChunks, static_cast<int>(0.35 * avg));
-    // A split sequence has P = ceil(c / L) >= 3 segments, so P < 1.5 c / L.
-    const int64_t cap = static_cast<int64_t>(1.6 * static_cast<double>(chunks) / sh.l_min) + 2;
+    // A split sequence has P = ceil(c / L) >= 2 segments (c > L), so P < 2 c / L.
+    const int64_t cap = static_cast<int64_t>(2.1 * static_cast<double>(chunks) / sh.l_min) + 2;
     const int64_t budget = static_cast<int64_t>(
         kSplitStateBudget / (3 * static_cast<size_t>(p.heads_v) * kD * kD * sizeof(float)));
     sh.seg_cap = static_cast<int>(std::max<int64_t>(3, std::min(cap, budget)));
@@ -1936,7 +1940,7 @@ cudaError_t launch_chunked_split(const Problem& p, const void* q, const void* k,
     const SplitShape sh = split_shape(p, forced);
     const size_t cap_a = static_cast<size_t>(p.n_seqs) + 2 * static_cast<size_t>(sh.seg_cap);
     const size_t cap_b = static_cast<size_t>(sh.seg_cap);
-    const size_t cap_s = static_cast<size_t>(sh.seg_cap) / 3 + 1;
+    const size_t cap_s = static_cast<size_t>(sh.seg_cap) / 2 + 1;  // >= 2 segments each
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
     const size_t off_a = up(kSplitHeader * sizeof(int32_t));
     const size_t off_b = off_a + up(cap_a * sizeof(SplitDesc));
