@@ -238,7 +238,31 @@ conv_vec_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ wei
     }
 }
 
-// bf16 with C and the split points multiples of 8: a CTA walks kStageSpan
+// Two 16-bit values packed in a word, as f32 pairs.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// bf16 or f16 with C and the split points multiples of 8: a CTA walks kStageSpan
 // positions of 1024 channels (eight per thread, one 16-byte load and store per
 // position), the rows of each 16-position window staged into shared memory by
 // cp.async while the window before is computed, so the loads stay in flight
@@ -252,14 +276,13 @@ constexpr int kStageRows = 16, kStageCh = 8, kStageCols = kConvThreads * kStageC
               kStageSpan = 512;
 constexpr uint32_t kStageBytes = 2u * kStageRows * kStageCols * 2;  // two windows
 
-template <int K, bool kSilu>
+template <typename T, int K, bool kSilu>
 __global__ void __launch_bounds__(kConvThreads, K <= 4 ? 4 : 2)
-conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
-                   const __nv_bfloat16* __restrict__ weight, const float* state,
-                   __nv_bfloat16* out0, __nv_bfloat16* out1, __nv_bfloat16* out2) {
+conv_staged_kernel(const Conv p, const T* __restrict__ x, const T* __restrict__ weight,
+                   const float* state, T* out0, T* out1, T* out2) {
     constexpr int NP = kStageCh / 2;  // channel pairs per thread
     extern __shared__ __align__(16) uint8_t conv_smem[];
-    auto* buf = reinterpret_cast<__nv_bfloat16*>(conv_smem);  // [2][16][1024]
+    auto* buf = reinterpret_cast<T*>(conv_smem);  // [2][16][1024]
     const int C = p.channels, tid = threadIdx.x;
     const int cb = blockIdx.x * kStageCols;
     const int c0 = cb + kStageCh * tid;
@@ -268,14 +291,14 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
     const int64_t T1 = T0 + kStageSpan < p.tokens ? T0 + kStageSpan : p.tokens;
     const int windows = static_cast<int>((T1 - T0 + kStageRows - 1) / kStageRows);
     auto load_window = [&](int w) {  // kStageRows rows x 128 16-byte pieces
-        __nv_bfloat16* dst = buf + (w & 1) * kStageRows * kStageCols;
+        T* dst = buf + (w & 1) * kStageRows * kStageCols;
 #pragma unroll 4
         for (int e = tid; e < kStageRows * (kStageCols / 8); e += kConvThreads) {
             const int r = e / (kStageCols / 8), piece = e % (kStageCols / 8);
             const int64_t t = T0 + static_cast<int64_t>(w) * kStageRows + r;
             const int c = cb + 8 * piece;
             const bool in = t < T1 && c < C;
-            const __nv_bfloat16* src = x + (in ? t * C + c : 0);
+            const T* src = x + (in ? t * C + c : 0);
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
                              static_cast<uint32_t>(__cvta_generic_to_shared(dst + r * kStageCols + 8 * piece))),
                          "l"(src), "r"(in ? 16 : 0)
@@ -289,7 +312,7 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
     float2 h[NP][K - 1];  // the K - 1 inputs before the current position
     int s = 0;
     int64_t start = 0, end = 0;
-    __nv_bfloat16* out = nullptr;
+    T* out = nullptr;
     int64_t stride = 0;
     int col = 0;
     if (active) {
@@ -331,7 +354,7 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
         }
         __syncthreads();  // window wi has landed for every thread
         if (active) {
-            const __nv_bfloat16* rows = buf + (wi & 1) * kStageRows * kStageCols + kStageCh * tid;
+            const T* rows = buf + (wi & 1) * kStageRows * kStageCols + kStageCh * tid;
             const int64_t tw = T0 + static_cast<int64_t>(wi) * kStageRows;
             const int n = static_cast<int>(T1 - tw < kStageRows ? T1 - tw : kStageRows);
             int r = 0;
@@ -358,8 +381,7 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
                     uint32_t y[NP];
 #pragma unroll
                     for (int q = 0; q < NP; ++q) {
-                        const float2 xt =
-                            __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[q]));
+                        const float2 xt = unpack2<T>(xw[q]);
                         float a0 = h[q][0].x * w[q][0].x, a1 = h[q][0].y * w[q][0].y;
 #pragma unroll
                         for (int j = 1; j < K - 1; ++j) {
@@ -372,8 +394,7 @@ conv_staged_kernel(const Conv p, const __nv_bfloat16* __restrict__ x,
                             a0 = silu(a0);
                             a1 = silu(a1);
                         }
-                        const __nv_bfloat162 yq = __floats2bfloat162_rn(a0, a1);
-                        y[q] = *reinterpret_cast<const uint32_t*>(&yq);
+                        y[q] = pack2<T>(a0, a1);
 #pragma unroll
                         for (int i = 0; i + 1 < K - 1; ++i) h[q][i] = h[q][i + 1];
                         h[q][K - 2] = xt;
@@ -547,20 +568,19 @@ void launch_conv_k(const Conv& p, const void* x, const void* w, const float* st,
     const bool vec = p.channels % 2 == 0 && p.split0 % 2 == 0 && p.split1 % 2 == 0 &&
                      (al & 7) == 0;
     const unsigned ty = static_cast<unsigned>((p.tokens + kConvTokens - 1) / kConvTokens);
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value) {
         const uintptr_t al16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(o0) |
                                reinterpret_cast<uintptr_t>(o1) | reinterpret_cast<uintptr_t>(o2);
         if (vec && p.channels % kStageCh == 0 && p.split0 % kStageCh == 0 &&
             p.split1 % kStageCh == 0 && (al16 & 15) == 0) {
-            auto* kern = p.silu ? conv_staged_kernel<K, true> : conv_staged_kernel<K, false>;
+            auto* kern = p.silu ? conv_staged_kernel<T, K, true> : conv_staged_kernel<T, K, false>;
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kStageBytes));
             const dim3 grid((p.channels + kStageCols - 1) / kStageCols,
                             static_cast<unsigned>((p.tokens + kStageSpan - 1) / kStageSpan));
             kern<<<grid, kConvThreads, kStageBytes, s>>>(
-                p, static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), st,
-                static_cast<__nv_bfloat16*>(o0), static_cast<__nv_bfloat16*>(o1),
-                static_cast<__nv_bfloat16*>(o2));
+                p, static_cast<const T*>(x), static_cast<const T*>(w), st, static_cast<T*>(o0),
+                static_cast<T*>(o1), static_cast<T*>(o2));
             return;
         }
     }

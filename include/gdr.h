@@ -182,7 +182,7 @@ gdr_status gdr_chunked_host(const gdr_params* params, const void* q, const void*
  * (the layer's q / k / v split; split0 = split1 = C writes one [.., C]
  * output). `silu` applies the layer's activation. state_out (NULL: none) gets
  * the last K - 1 inputs of [state, x] and may equal state_in. Any shape runs;
- * bf16 with C, split0 and split1 multiples of 8, x and the outputs 16-byte
+ * bf16 or f16 with C, split0 and split1 multiples of 8, x and the outputs 16-byte
  * aligned and the states 8-byte aligned takes the fast kernel (eight channels
  * per thread, 16-byte accesses), the layer's own shapes among them. */
 typedef struct gdr_conv_params {

@@ -49,25 +49,26 @@ def test_conv_packed_against_oracle(dtype, taps, with_state, c):
     assert np.array_equal(_np(nxt), want_next)  # the inputs themselves, exactly
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("silu", [True, False])
 @pytest.mark.parametrize("splits", [(264, 528), (66, 132)])  # 8-channel threads / 2-channel
-def test_conv_bf16_across_spans_and_column_blocks(silu, splits):
-    """bf16 with positions past one CTA's 512 (windows whose history comes from
-    x), sequences starting inside a window, 1032 channels (a second, mostly idle
-    block of 1024) and state for every sequence."""
+def test_conv_16bit_across_spans_and_column_blocks(dtype, silu, splits):
+    """bf16 and f16 with positions past one CTA's 512 (windows whose history
+    comes from x), sequences starting inside a window, 1032 channels (a second,
+    mostly idle block of 1024) and state for every sequence."""
     gen = torch.Generator(device=DEV).manual_seed(17)
     lens = [700, 1, 0, 900, 5, 31, 17, 500]
     c, taps = 1032, 4
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=DEV)
-    x = torch.randn(sum(lens), c, device=DEV, generator=gen).bfloat16()
-    w = (torch.randn(c, taps, device=DEV, generator=gen) * 0.5).bfloat16()
-    s0 = torch.randn(len(lens), taps - 1, c, device=DEV, generator=gen).bfloat16().float()
+    x = torch.randn(sum(lens), c, device=DEV, generator=gen).to(dtype)
+    w = (torch.randn(c, taps, device=DEV, generator=gen) * 0.5).to(dtype)
+    s0 = torch.randn(len(lens), taps - 1, c, device=DEV, generator=gen).to(dtype).float()
     (q, k, v), nxt = causal_conv1d(x, w, s0, cu_seqlens=cu, silu=silu, splits=splits)
     _ok()
     want, want_next = olayer.causal_conv1d(_np(x), _np(w), _np(s0), cu_seqlens=_np(cu).astype(
         np.int32), activation=silu)
     got = np.concatenate([_np(q), _np(k), _np(v)], axis=1)
-    assert rel_err(got, want) < TOL_BF16_OUT
+    assert rel_err(got, want) < (TOL_BF16_OUT if dtype == torch.bfloat16 else 2e-3)
     assert np.array_equal(_np(nxt), want_next)
 
 
